@@ -1,0 +1,466 @@
+#!/usr/bin/env python
+"""Sparse-MLA forward benchmark on B200 (one process per GPU).
+
+``python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME]
+[--variant uniform|peaked|duplicates] [--impl ours|reference]``
+
+A step is one full ``dsa_b200.forward`` call (main kernel + merge when
+split > 1) over the config's synthetic inputs. With N ranks (torchrun), the
+flattened B*SQ queries are sharded contiguously (kv replicated per rank);
+each rank times only its own forward calls; the reported time is the max
+over ranks. The output all-gather runs after the timed region.
+
+Default workload: ``prefill_h128`` (B=4, SQ=4096, H=128, L=65536,
+TOPK=2048), the benchmark config that is partitioned across 1/2/4/8 B200.
+Total work is fixed as N grows ("strong" scaling).
+
+``--impl reference`` times the reference's own FP32 math (the CPU oracle,
+tools/review.py:123-145 of CHNJZ/dsa) on all host cores, on a bounded
+sample of the same workload per step, scaled to a full call.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "sparse-MLA fwd µs/call, HBM GB/s & TFLOP/s vs roofline at 1/2/4/8 B200"
+SEED = 20261103
+
+# name -> (B, SQ, H, L, TOPK); BASELINE.json configs[0..4]
+CONFIGS = {
+    "decode_b1": (1, 1, 128, 4096, 2048),
+    "decode_b8": (8, 2, 128, 32768, 2048),
+    "decode_tp8": (64, 1, 16, 65536, 2048),
+    "prefill_tp8": (1, 4096, 16, 8192, 2048),
+    "prefill_h128": (4, 4096, 128, 65536, 2048),
+}
+DEFAULT_CONFIG = "prefill_h128"
+
+# Dominant-kernel DRAM traffic per launch (dram__bytes_read.sum +
+# dram__bytes_write.sum) from the ncu captures summarised under profiles/;
+# None until a capture of that kernel/config exists.
+TRAFFIC_BYTES = {}
+
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def algorithmic(shape):
+    """Per-call algorithmic work: gathered bytes Q*TOPK*1152, other bytes
+    (q, q_rope, output, stats, indices) and FLOPs Q*H*2*TOPK*1088."""
+    b, s, h, _, k = shape
+    q = b * s
+    gathered = q * k * 1152
+    other = q * h * (512 + 64) * 2 + q * h * 512 * 2 + q * h * 8 + q * k * 4
+    flops = q * h * 2 * k * 1088
+    return gathered, other, flops
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Synthetic inputs (seeded, generated on the device; same shapes and value
+# distributions as the configs: N(0,1) BF16 tensors, int32 indices).
+# ---------------------------------------------------------------------------
+def make_device_indices(batch, queries, length, topk, seed, variant, device):
+    g = torch.Generator(device=device).manual_seed(seed + 1)
+    rows = batch * queries
+    out = torch.empty((rows, topk), dtype=torch.int32, device=device)
+    if variant in ("uniform", "duplicates"):
+        chunk = max(1, (256 << 20) // (length * 4))
+        for r0 in range(0, rows, chunk):
+            r1 = min(rows, r0 + chunk)
+            keys = torch.rand((r1 - r0, length), generator=g, device=device)
+            out[r0:r1] = keys.argsort(dim=-1)[:, :topk].int()
+        if variant == "duplicates":
+            n_dup = int(round(0.1 * topk))
+            gc = torch.Generator().manual_seed(seed + 2)
+            host = out.cpu()
+            for r in range(rows):
+                slots = (torch.randperm(topk - 1, generator=gc)[:n_dup] + 1).sort().values.tolist()
+                row = host[r]
+                for slot in slots:
+                    row[slot] = row[int(torch.randint(0, slot, (1,), generator=gc))]
+            out.copy_(host)
+    elif variant == "peaked":
+        recent = min(4096, length)
+        n_hot = min(int(round(0.7 * topk)), recent)
+        n_cold = topk - n_hot
+        hot = torch.rand((rows, recent), generator=g, device=device).argsort(-1)[:, :n_hot] + (length - recent)
+        cold = torch.rand((rows, length - recent), generator=g, device=device).argsort(-1)[:, :n_cold]
+        out.copy_(torch.cat([hot, cold], dim=1).int())
+    else:
+        raise ValueError(variant)
+    return out.reshape(batch, queries, 1, topk)
+
+
+def make_device_inputs(shape, seed=SEED, variant="uniform", device="cuda"):
+    b, s, h, length, k = shape
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def normal(*dims):
+        t = torch.empty(dims, dtype=torch.bfloat16, device=device)
+        flat = t.view(-1)
+        step = 1 << 28
+        for i in range(0, flat.numel(), step):
+            n = min(step, flat.numel() - i)
+            flat[i:i + n] = torch.randn(n, generator=g, device=device).bfloat16()
+        return t
+
+    q = normal(b, s, h, 512)
+    kv = normal(b, length, 1, 512)
+    q_rope = normal(b, s, h, 64)
+    k_rope = normal(b, length, 1, 64)
+    ids = make_device_indices(b, s, length, k, seed, variant, device)
+    return q, kv, q_rope, k_rope, ids
+
+
+def compact_for_oracle(data, rows):
+    """CPU copies of the inputs restricted to flattened query ``rows``, with
+    each query's selected kv rows gathered into its own compact batch
+    (L' = TOPK, indices remapped, invalid ones kept invalid). The oracle's
+    arithmetic on the compact problem is identical to the full one."""
+    q, kv, q_rope, k_rope, ids = data
+    b, s, h, _ = q.shape
+    length = kv.shape[1]
+    rows_t = torch.as_tensor(rows, device=q.device, dtype=torch.long)
+    bi = rows_t // s
+    si = rows_t % s
+    idx = ids[bi, si, 0].long()                       # [n, K]
+    valid = (idx >= 0) & (idx < length)
+    safe = idx.clamp(0, length - 1)
+    kv_c = kv[bi[:, None], safe, 0]                  # [n, K, 512]
+    kr_c = k_rope[bi[:, None], safe, 0]
+    k = idx.shape[1]
+    ids_c = torch.arange(k, device=q.device, dtype=torch.int32).expand(len(rows), k).clone()
+    ids_c[~valid] = -1
+    return (q[bi, si].unsqueeze(1).cpu(), kv_c.unsqueeze(2).cpu(), q_rope[bi, si].unsqueeze(1).cpu(),
+            kr_c.unsqueeze(2).cpu(), ids_c.reshape(len(rows), 1, 1, k).cpu())
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        # Address the GPU by UUID so the sample follows the CUDA device even
+        # when CUDA_VISIBLE_DEVICES renumbers devices.
+        try:
+            uuid = str(torch.cuda.get_device_properties(gpu_index).uuid)
+            self.gpu_index = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:  # noqa: BLE001 - fall back to the ordinal
+            self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------
+# CPU reference (oracle) timing
+# ---------------------------------------------------------------------------
+def cpu_reference_rate(data, shape, budget_s, max_rows=None):
+    """Time the oracle on consecutive query rows until ``budget_s`` elapses;
+    returns (seconds per full call, rows timed, threads)."""
+    from oracle import sparse_mla as oracle  # checker/baseline only
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    b, s, h, _, k = shape
+    total = b * s
+    chunk = max(1, min(total, 16 if h >= 64 else 128))
+    rows_done, elapsed = 0, 0.0
+    while rows_done < total and elapsed < budget_s and (max_rows is None or rows_done < max_rows):
+        rows = list(range(rows_done, min(total, rows_done + chunk)))
+        compact = compact_for_oracle(data, rows)
+        t0 = time.perf_counter()
+        oracle.reference_forward(*compact)
+        elapsed += time.perf_counter() - t0
+        rows_done += len(rows)
+    return elapsed / rows_done * total, rows_done, torch.get_num_threads()
+
+
+# ---------------------------------------------------------------------------
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def run_reference(args, shape):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    data = make_device_inputs(shape, SEED, args.variant, dev)
+    b, s, h, length, k = shape
+    total = b * s
+    sample_rows = min(total, {16: 512, 32: 256, 64: 128, 128: 64}.get(h, 64))
+    per_call = []
+    for i in range(args.warmup + args.steps):
+        t, rows, threads = cpu_reference_rate(data, shape, budget_s=1e9, max_rows=sample_rows)
+        if i >= args.warmup:
+            per_call.append(t)
+    us = statistics.mean(per_call) * 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": us, "unit": "us/call", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, "B": b, "SQ": s, "H": h, "L": length, "TOPK": k,
+                   "index_variant": args.variant, "seed": SEED},
+        "cpu_baseline": {"value": us, "unit": "us/call", "cores": threads, "kind": "port",
+                         "sample": f"{sample_rows} of {total} queries per step (FP32 torch oracle of "
+                                   f"tools/review.py:123-145, HF32/TF32 off), scaled to a full call"},
+        "e2e": {"value": us, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
+    ap.add_argument("--variant", default="uniform", choices=("uniform", "peaked", "duplicates"))
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    shape = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, shape)
+
+    import dsa_b200
+    from dsa_b200 import _native, sharded
+
+    world, rank, local = init_dist()
+    device = torch.device("cuda", local)
+    b, s, h, length, k = shape
+    data = make_device_inputs(shape, SEED, args.variant, device)
+    lo, hi = sharded.shard_bounds(b * s, world, rank)
+    pieces = sharded.shard_pieces(s, lo, hi)
+    views = [(data[0][b0:b1, s0:s1], data[1][b0:b1], data[2][b0:b1, s0:s1], data[3][b0:b1],
+              data[4][b0:b1, s0:s1]) for b0, b1, s0, s1 in pieces]
+    lib = _native.load()
+
+    def step():
+        launches = 0
+        res = None
+        for v in views:
+            res = dsa_b200.forward(*v)
+            launches += lib.dsa_last_launch_count()
+        return res, launches
+
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches_total = 0
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(float(i))  # evict L2 between timed iterations (outside the events)
+            starts[i].record(stream)
+            _, n = step()
+            ends[i].record(stream)
+            launches_total += n
+        torch.cuda.synchronize()
+    durations = [a.elapsed_time(e) for a, e in zip(starts, ends)]  # ms
+    total_ms = sum(durations)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+
+    # End-to-end through the public API: pinned host inputs -> device, forward,
+    # outputs -> pinned host, every step.
+    e2e_steps = args.e2e_steps or max(1, min(args.steps, 5))
+    host_in = [t.cpu().pin_memory() for t in data]
+    dev_in = [torch.empty_like(t) for t in data]
+    out_host = None
+    h2d_bytes = sum(t.numel() * t.element_size() for t in host_in)
+    data = None
+    views = None
+
+    def e2e_step():
+        nonlocal out_host
+        for hsrc, ddst in zip(host_in, dev_in):
+            ddst.copy_(hsrc, non_blocking=True)
+        vws = [(dev_in[0][b0:b1, s0:s1], dev_in[1][b0:b1], dev_in[2][b0:b1, s0:s1], dev_in[3][b0:b1],
+                dev_in[4][b0:b1, s0:s1]) for b0, b1, s0, s1 in pieces]
+        outs = [dsa_b200.forward(*v) for v in vws]
+        if out_host is None:
+            out_host = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in o] for o in outs]
+        for o, hdst in zip(outs, out_host):
+            for t, hd in zip(o, hdst):
+                hd.copy_(t, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    d2h_bytes = sum(t.numel() * t.element_size() for o in out_host for t in o)
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    gathered, other, flops = algorithmic(shape)
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    us = ms_per_step * 1e3
+    # Roofline of the dominant kernel (the main kernel; for split == 1 configs
+    # it is the only launch per call, so the per-call events time it).
+    rank_share = (hi - lo) / (b * s)
+    per_launch_flops = flops * rank_share
+    per_launch_bytes = gathered * rank_share
+    if h >= 64:
+        bound, achieved, peak, unit = "tensor", per_launch_flops / (ms_per_step * 1e-3) / 1e12, tf_peak, "TFLOP/s"
+    else:
+        bound, achieved, peak, unit = "hbm", per_launch_bytes / (ms_per_step * 1e-3) / 1e9, hbm_peak, "GB/s"
+    line = {
+        "metric": METRIC,
+        "value": us,
+        "unit": "us/call",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) BF16 q/kv/q_rope/k_rope, int32 top-k indices "
+                f"({args.variant}), generated on the device",
+        "config": {"workload": args.config, "B": b, "SQ": s, "H": h, "L": length, "TOPK": k,
+                   "index_variant": args.variant, "seed": SEED,
+                   "parallelism": f"query-shard x{world}, kv replicated",
+                   "l2": "flushed between timed iterations (256 MiB write outside the events)"},
+        "calls_per_s": 1e6 / us,
+        "tflops": flops / (us * 1e-6) / 1e12,
+        "gathered_gbs": gathered / (us * 1e-6) / 1e9,
+        "step_ms_p10_p50_p90": [statistics.quantiles(durations, n=10)[0] if len(durations) > 1 else durations[0],
+                                statistics.median(durations),
+                                statistics.quantiles(durations, n=10)[-1] if len(durations) > 1 else durations[0]],
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)",
+                     "traffic": TRAFFIC_BYTES.get(args.config)},
+        "e2e": {"value": e2e_ms * 1e3, "unit": "us/call", "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": d2h_bytes, "steps": e2e_steps},
+        "gpu_launches": launches_total,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dev_data = [t.to(device, non_blocking=True) for t in host_in]
+        torch.cuda.synchronize()
+        sec, rows, threads = cpu_reference_rate(dev_data, shape, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": sec * 1e6, "unit": "us/call", "cores": threads, "kind": "port",
+                                "sample": f"first {rows} of {b * s} queries (~{args.cpu_budget:.0f} s), "
+                                          "FP32 torch oracle, scaled to a full call"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

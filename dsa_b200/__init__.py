@@ -1,0 +1,9 @@
+"""B200 (sm_100a) sparse-MLA attention forward with the CHNJZ/dsa API.
+
+Drop-in for ``dsa.forward`` (dsa/__init__.py:2-5 of the reference):
+``import dsa_b200 as dsa; dsa.forward(q, kv, q_rope, k_rope, indices)``.
+"""
+from .api import device_status, forward
+from .config import CASE_SHAPES, SELECTED, Tuning
+
+__all__ = ["forward", "Tuning", "CASE_SHAPES", "SELECTED", "device_status"]

@@ -1,0 +1,183 @@
+"""Public entry point: check inputs, pick the launch entry, allocate, launch.
+
+Mirrors ``forward`` of CHNJZ/dsa (dsa/api.py:81-137) on CUDA tensors:
+same signature, same input contract (dsa/api.py:23-43), same outputs and the
+same exception types. The device work is the sm_100a library
+(libdsa_b200.so, include/dsa_b200.h) reached through ctypes; there is no
+Python, Triton or CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from collections import namedtuple
+
+import torch
+
+from . import _native
+from .config import Tuning, select
+
+# Device type the inputs must live on. Host-contract tests set it to "meta"
+# (as tools/check_host_api.py:58 does for "npu") together with a stub
+# launcher; product code never changes it.
+DEVICE_TYPE = "cuda"
+
+LaunchRecord = namedtuple("LaunchRecord", "name family heads_per_cta keys_per_tile split")
+
+_FAMILY_NAMES = {_native.FAMILY_WARP_MMA: "warp_mma", _native.FAMILY_UMMA: "umma"}
+
+
+def _check_inputs(q, kv, q_rope, k_rope, indices):
+    """Shape/device/contiguity/dtype contract of dsa/api.py:23-43."""
+    q_shape, kv_shape, ids_shape = q.shape, kv.shape, indices.shape
+    if len(q_shape) != 4 or len(kv_shape) != 4 or len(ids_shape) != 4:
+        raise ValueError("q, kv and indices must be 4-D tensors")
+    batch, queries, heads, width = q_shape
+    length, topk = kv_shape[1], ids_shape[-1]
+    if (width != 512 or kv_shape != (batch, length, 1, 512) or q_rope.shape != (batch, queries, heads, 64)
+            or k_rope.shape != (batch, length, 1, 64) or ids_shape != (batch, queries, 1, topk)
+            or min(batch, queries, heads, length, topk) <= 0):
+        raise ValueError("need q[B,SQ,H,512], kv[B,L,1,512], q_rope/k_rope with 64 dims, indices[B,SQ,1,K]")
+    device = q.device
+    if (device.type != DEVICE_TYPE or kv.device != device or q_rope.device != device
+            or k_rope.device != device or indices.device != device or not q.is_contiguous()
+            or not kv.is_contiguous() or not q_rope.is_contiguous() or not k_rope.is_contiguous()
+            or not indices.is_contiguous()):
+        raise ValueError("all inputs must be contiguous and on the same CUDA device")
+    bf16 = torch.bfloat16
+    if (q.dtype != bf16 or kv.dtype != bf16 or q_rope.dtype != bf16 or k_rope.dtype != bf16
+            or indices.dtype != torch.int32):
+        raise ValueError("q/kv/q_rope/k_rope must be bfloat16 and indices int32")
+    return (batch, queries, heads, length, topk), device
+
+
+def _check_cores(cores):
+    # Accepted for source compatibility (dsa/api.py:81, :99-100); the grid is
+    # sized from the device's SM count, so the value is only validated.
+    if type(cores) is not int or cores <= 0:
+        raise ValueError("cores must be a positive int")
+
+
+def _check_tuning(config, shape, cores):
+    """Launch-entry checks: the reference's field rules (dsa/api.py:46-65)
+    plus what the sm_100a kernels support (dsa_check_launch)."""
+    if not isinstance(config, Tuning):
+        raise TypeError("config must be a dsa_b200.Tuning")
+    _, _, heads, _, _ = shape
+    _check_cores(cores)
+    if any(type(v) is not int or v <= 0 for v in (config.bm, config.bn, config.split, config.pv_cols)):
+        raise ValueError("bm/bn/split/pv_cols must be positive ints")
+    if config.bm not in (16, 32, 64, 128) or heads % config.bm:
+        raise ValueError("bm must be 16/32/64/128 and divide the head count")
+    if config.pv_cols not in (128, 256, 512):
+        raise ValueError("pv_cols must be 128/256/512")
+
+
+def _launch_from_tuning(config, shape):
+    launch = _native.Launch(_native.FAMILY_WARP_MMA, 16, config.bn, config.split)
+    code = _native.load().dsa_check_launch(*shape, ctypes.byref(launch))
+    if code != _native.STATUS_OK:
+        raise ValueError(f"Tuning {config} is not supported on sm_100a for shape {shape}: "
+                         f"{_native.status_string(code)}")
+    return launch
+
+
+_default_cache = {}
+
+
+def _default_launch(shape, device):
+    key = (shape, device.index)
+    launch = _default_cache.get(key)
+    if launch is None:
+        tuned = select(shape)
+        if tuned is not None:
+            launch = _launch_from_tuning(tuned, shape)
+        else:
+            launch = _native.Launch()
+            code = _native.load().dsa_default_launch(*shape, ctypes.byref(launch))
+            _native.raise_for_status(code, f"no launch entry for shape {shape}")
+        _default_cache[key] = launch
+    return launch
+
+
+_status_words = {}
+
+
+def _status_word(device):
+    word = _status_words.get(device.index)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=device)
+        _status_words[device.index] = word
+    return word
+
+
+def device_status(device=None) -> int:
+    """Synchronise and return the OR of device error bits reported so far
+    (1 = a bounded device-side wait timed out)."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    word = _status_word(device)
+    torch.cuda.synchronize(device)
+    return int(word.item())
+
+
+def _launch_native(args, stream_handle):
+    """Enqueue the forward through the C ABI; returns the kernel count."""
+    lib = _native.load()
+    code = lib.dsa_sparse_mla_fwd(ctypes.byref(args), stream_handle)
+    _native.raise_for_status(code, "dsa_sparse_mla_fwd")
+    return lib.dsa_last_launch_count()
+
+
+def _workspace_bytes(args):
+    return int(_native.load().dsa_fwd_workspace_bytes(ctypes.byref(args)))
+
+
+def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_kernels=False):
+    """Sparse MLA attention with given top-k indices.
+
+    Returns ``(output, softmax_max, softmax_sum)``: output BF16
+    ``[B,SQ,H,512]``; the two statistics FP32 ``[B,1,SQ,H]`` (natural-exp
+    max and sum of the scaled scores). The scale is fixed at 1/sqrt(512+64).
+    Duplicate indices keep their repeated weight; indices outside [0, L) are
+    masked. Every query needs at least one valid index (dsa/api.py:82-91).
+
+    ``config`` overrides the shape-keyed launch entry; ``cores`` is validated
+    for compatibility; ``return_kernels=True`` returns
+    ``(outputs, launch_records)`` describing the enqueued kernels.
+    Work is enqueued on ``torch.cuda.current_stream()``; nothing synchronises.
+    """
+    shape, device = _check_inputs(q, kv, q_rope, k_rope, indices)
+    if config is None:
+        _check_cores(cores)
+        launch = _default_launch(shape, device)
+    else:
+        _check_tuning(config, shape, cores)
+        launch = _launch_from_tuning(config, shape)
+    batch, queries, heads, length, topk = shape
+
+    output = torch.empty_like(q)
+    maximum = torch.empty((batch, 1, queries, heads), device=device, dtype=torch.float32)
+    denominator = torch.empty_like(maximum)
+
+    args = _native.FwdArgs()
+    args.q, args.kv, args.q_rope, args.k_rope = q.data_ptr(), kv.data_ptr(), q_rope.data_ptr(), k_rope.data_ptr()
+    args.indices = indices.data_ptr()
+    args.output, args.softmax_max, args.softmax_sum = output.data_ptr(), maximum.data_ptr(), denominator.data_ptr()
+    args.batch, args.queries, args.heads, args.length, args.topk = shape
+    args.launch = launch
+    ws_bytes = _workspace_bytes(args)
+    workspace = None
+    if ws_bytes:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        args.workspace, args.workspace_bytes = workspace.data_ptr(), ws_bytes
+    args.status = _status_word(device).data_ptr()
+    stream = torch.cuda.current_stream(device).cuda_stream if DEVICE_TYPE == "cuda" else 0
+    count = _launch_native(args, stream)
+    result = (output, maximum, denominator)
+    if return_kernels:
+        name = "dsa_fwd_" + _FAMILY_NAMES.get(launch.family, str(launch.family))
+        records = [LaunchRecord(name, launch.family, launch.heads_per_cta, launch.keys_per_tile, launch.split)]
+        if count > 1:
+            records.append(LaunchRecord("dsa_merge", launch.family, launch.heads_per_cta,
+                                        launch.keys_per_tile, launch.split))
+        return result, tuple(records)
+    return result

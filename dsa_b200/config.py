@@ -1,0 +1,90 @@
+"""Shape-keyed sm_100a launch table (mirrors dsa/config.py of CHNJZ/dsa).
+
+Dispatch depends only on tensor shapes, never on input values, seeds or
+reference results (the rule of dsa/config.py:3).
+
+``Tuning`` keeps the reference's fields and defaults (dsa/config.py:10-19) so
+that existing callers can still pass ``config=Tuning(...)``. Their meaning on
+B200:
+
+* ``bm`` — heads that share one gathered KV tile. ``bm == 128`` selects the
+  tcgen05/TMEM family (one 2-CTA cluster per query for H = 128) once that
+  family is built; any other legal ``bm`` selects the generic warp-MMA family,
+  whose CTAs each own 16 heads.
+* ``bn`` — selected KV rows per pipeline stage (32 or 64 for warp-MMA).
+* ``split`` — KV splits per (query, head tile); ``split > 1`` writes FP32
+  partials to the workspace and runs the FP32 merge (dsa/merge.py).
+* ``direct_nz``, ``pv_cols``, ``share_score`` — Ascend data-movement knobs
+  (NZ packing, PV fragment width, score/PV UB sharing) with no counterpart on
+  sm_100a. They are type-checked as in the reference but do not change the
+  launch.
+
+``CASE_SHAPES`` holds the reference's 16 shapes (dsa/config.py:23-40) and the
+five benchmark configs of this build. ``SELECTED`` maps every name to the
+entry used for it. Unlike the reference (dsa/config.py:64-69), a shape that
+is not in the table is not rejected: ``select`` returns the library's
+shape-only heuristic entry for it.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+
+@dataclass(frozen=True)
+class Tuning:
+    """Launch entry; the fields are the reference's (dsa/config.py:10-19)."""
+
+    bm: int
+    bn: int
+    split: int
+    direct_nz: bool = False
+    pv_cols: int = 512
+    share_score: bool = False
+
+
+# (batch, query length, heads, KV length, number of selected indices)
+CASE_SHAPES = {
+    # the reference's validated shapes (dsa/config.py:23-40)
+    "decode_b1": (1, 1, 128, 8192, 2048),
+    "decode_b8": (8, 1, 128, 32768, 2048),
+    "decode_b32": (32, 1, 128, 32768, 2048),
+    "decode_tp8": (8, 1, 16, 32768, 2048),
+    "prefill_q16": (1, 16, 128, 8192, 2048),
+    "prefill_q64": (1, 64, 128, 32768, 2048),
+    "prefill_tp8": (1, 128, 16, 32768, 2048),
+    "prefill_k512": (1, 128, 64, 32768, 512),
+    "decode_b4_h128": (4, 1, 128, 8192, 2048),
+    "prefill_b4_h128": (4, 8192, 128, 8192, 2048),
+    "decode_b4_h64": (4, 1, 64, 8192, 2048),
+    "prefill_b4_h64": (4, 8192, 64, 8192, 2048),
+    "decode_b4_h32": (4, 1, 32, 8192, 2048),
+    "prefill_b4_h32": (4, 8192, 32, 8192, 2048),
+    "decode_b4_h16": (4, 1, 16, 8192, 2048),
+    "prefill_b4_h16": (4, 8192, 16, 8192, 2048),
+    # the B200 benchmark configs
+    "bench_decode_b1": (1, 1, 128, 4096, 2048),
+    "bench_decode_b8": (8, 2, 128, 32768, 2048),
+    "bench_decode_tp8": (64, 1, 16, 65536, 2048),
+    "bench_prefill_tp8": (1, 4096, 16, 8192, 2048),
+    "bench_prefill_h128": (4, 4096, 128, 65536, 2048),
+}
+
+# Tuned entries per named shape. Shapes absent here use the library heuristic
+# (dsa_default_launch in dsa_b200/csrc/dsa_capi.cu).
+SELECTED: dict = {}
+
+_BY_SHAPE = {}
+
+
+def _rebuild_index():
+    _BY_SHAPE.clear()
+    for name, tuning in SELECTED.items():
+        _BY_SHAPE[CASE_SHAPES[name]] = tuning
+
+
+_rebuild_index()
+
+
+def select(shape):
+    """Tuned entry for ``shape`` or ``None`` (=> the library's heuristic)."""
+    return _BY_SHAPE.get(tuple(shape))

@@ -1,0 +1,220 @@
+// extern "C" boundary of libdsa_b200.so (declared in include/dsa_b200.h).
+//
+// Host-side orchestration of one forward call, the C++ counterpart of the
+// reference's forward (dsa/api.py:81-137): pick or check the launch entry,
+// carve the split partials out of the caller's workspace, launch the main
+// kernel and, for split > 1, the FP32 merge. Input validation of shapes and
+// dtypes happens in the Python mirror (dsa_b200/api.py); here only what the
+// C ABI can see is checked (null pointers, sizes, alignment, launch entry).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/dsa_b200.h"
+#include "dsa_common.cuh"
+
+namespace {
+
+thread_local int g_last_launch_count = 0;
+
+constexpr uint64_t kAlign = 256;
+inline uint64_t align_up(uint64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+bool shape_ok(int64_t b, int64_t sq, int64_t h, int64_t l, int64_t k) {
+  if (b <= 0 || sq <= 0 || h <= 0 || l <= 0 || k <= 0) return false;
+  if (b * sq > 0x7fffffffLL || l > 0x7fffffffLL || k > 0x7fffffffLL || h > 0x7fffffffLL) return false;
+  if (b * l > 0x7fffffffLL) return false;
+  return true;
+}
+
+struct Layout {
+  uint64_t num_off, max_off, sum_off, total;
+};
+
+Layout partial_layout(int64_t tokens, int64_t heads, int64_t split) {
+  Layout lay{0, 0, 0, 0};
+  if (split <= 1) return lay;
+  const uint64_t rows = (uint64_t)tokens * (uint64_t)split * (uint64_t)heads;
+  lay.num_off = 0;
+  lay.max_off = align_up(rows * dsa::kDimLatent * sizeof(float));
+  lay.sum_off = lay.max_off + align_up(rows * sizeof(float));
+  lay.total = lay.sum_off + align_up(rows * sizeof(float));
+  return lay;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int dsa_abi_version(void) { return DSA_B200_ABI_VERSION; }
+
+const char* dsa_status_string(int status) {
+  switch (status) {
+    case DSA_STATUS_OK: return "ok";
+    case DSA_STATUS_BAD_ARGUMENT: return "bad argument";
+    case DSA_STATUS_UNSUPPORTED: return "launch entry not supported for this shape";
+    case DSA_STATUS_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case DSA_STATUS_LAUNCH_FAILED: return "kernel launch failed";
+    case DSA_STATUS_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case DSA_STATUS_CUDA_ERROR: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t length, int64_t topk,
+                     const dsa_launch_t* launch) {
+  if (launch == nullptr || !shape_ok(batch, queries, heads, length, topk))
+    return DSA_STATUS_BAD_ARGUMENT;
+  const int bn = launch->keys_per_tile;
+  if (launch->split < 1) return DSA_STATUS_UNSUPPORTED;
+  switch (launch->family) {
+    case DSA_FAMILY_WARP_MMA: {
+      if (launch->heads_per_cta != 16 || heads % 16 != 0) return DSA_STATUS_UNSUPPORTED;
+      if (bn != 32 && bn != 64) return DSA_STATUS_UNSUPPORTED;
+      break;
+    }
+    default:
+      return DSA_STATUS_UNSUPPORTED;
+  }
+  const int64_t tiles = (topk + bn - 1) / bn;
+  if (launch->split > tiles) return DSA_STATUS_UNSUPPORTED;
+  return DSA_STATUS_OK;
+}
+
+int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t length, int64_t topk,
+                       dsa_launch_t* out) {
+  if (out == nullptr || !shape_ok(batch, queries, heads, length, topk))
+    return DSA_STATUS_BAD_ARGUMENT;
+  if (heads % 16 != 0) return DSA_STATUS_UNSUPPORTED;
+  dsa_launch_t e;
+  e.family = DSA_FAMILY_WARP_MMA;
+  e.heads_per_cta = 16;
+  e.keys_per_tile = 32;
+  // Enough CTAs for two full waves at two CTAs per SM; split the TOPK range
+  // only when the (token, head-group) jobs alone cannot fill the machine,
+  // keeping at least two tiles per split so the gather pipeline has depth.
+  const int64_t jobs = batch * queries * (heads / 16);
+  const int64_t target = 4LL * sm_count();
+  const int64_t tiles = (topk + e.keys_per_tile - 1) / e.keys_per_tile;
+  int64_t split = 1;
+  if (jobs < target) {
+    split = (target + jobs - 1) / jobs;
+    const int64_t cap = tiles / 2 > 0 ? tiles / 2 : 1;
+    if (split > cap) split = cap;
+  }
+  e.split = (int32_t)split;
+  *out = e;
+  return DSA_STATUS_OK;
+}
+
+uint64_t dsa_fwd_workspace_bytes(const dsa_fwd_args_t* a) {
+  if (a == nullptr) return 0;
+  dsa_launch_t e = a->launch;
+  if (e.family == DSA_FAMILY_AUTO &&
+      dsa_default_launch(a->batch, a->queries, a->heads, a->length, a->topk, &e) != DSA_STATUS_OK)
+    return 0;
+  if (dsa_check_launch(a->batch, a->queries, a->heads, a->length, a->topk, &e) != DSA_STATUS_OK)
+    return 0;
+  return partial_layout(a->batch * a->queries, a->heads, e.split).total;
+}
+
+int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
+  g_last_launch_count = 0;
+  if (a == nullptr) return DSA_STATUS_BAD_ARGUMENT;
+  if (!a->q || !a->kv || !a->q_rope || !a->k_rope || !a->indices || !a->output ||
+      !a->softmax_max || !a->softmax_sum)
+    return DSA_STATUS_BAD_ARGUMENT;
+  if (!aligned16(a->q) || !aligned16(a->kv) || !aligned16(a->q_rope) || !aligned16(a->k_rope) ||
+      !aligned16(a->output))
+    return DSA_STATUS_BAD_ARGUMENT;
+  dsa_launch_t e = a->launch;
+  if (e.family == DSA_FAMILY_AUTO) {
+    int st = dsa_default_launch(a->batch, a->queries, a->heads, a->length, a->topk, &e);
+    if (st != DSA_STATUS_OK) return st;
+  }
+  int st = dsa_check_launch(a->batch, a->queries, a->heads, a->length, a->topk, &e);
+  if (st != DSA_STATUS_OK) return st;
+
+  const int64_t tokens = a->batch * a->queries;
+  const Layout lay = partial_layout(tokens, a->heads, e.split);
+  if (lay.total > 0) {
+    if (a->workspace == nullptr || a->workspace_bytes < lay.total ||
+        (reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0)
+      return DSA_STATUS_WORKSPACE_TOO_SMALL;
+  }
+  char* ws = static_cast<char*>(a->workspace);
+
+  dsa::FwdParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.q = static_cast<const __nv_bfloat16*>(a->q);
+  p.kv = static_cast<const __nv_bfloat16*>(a->kv);
+  p.q_rope = static_cast<const __nv_bfloat16*>(a->q_rope);
+  p.k_rope = static_cast<const __nv_bfloat16*>(a->k_rope);
+  p.ids = a->indices;
+  p.out = static_cast<__nv_bfloat16*>(a->output);
+  p.out_max = a->softmax_max;
+  p.out_sum = a->softmax_sum;
+  if (e.split > 1) {
+    p.part_num = reinterpret_cast<float*>(ws + lay.num_off);
+    p.part_max = reinterpret_cast<float*>(ws + lay.max_off);
+    p.part_sum = reinterpret_cast<float*>(ws + lay.sum_off);
+  }
+  p.status = a->status;
+  p.batch = (int)a->batch;
+  p.queries = (int)a->queries;
+  p.heads = (int)a->heads;
+  p.length = (int)a->length;
+  p.topk = (int)a->topk;
+  p.tokens = (int)tokens;
+  p.split = e.split;
+  p.keys_per_tile = e.keys_per_tile;
+  p.heads_per_cta = e.heads_per_cta;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaSuccess;
+  switch (e.family) {
+    case DSA_FAMILY_WARP_MMA: err = dsa::launch_fwd_warp_mma(p, s); break;
+    default: return DSA_STATUS_UNSUPPORTED;
+  }
+  if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;
+  int launches = 1;
+  if (e.split > 1) {
+    err = dsa::launch_merge(p.part_num, p.part_max, p.part_sum, p.out, p.out_max, p.out_sum,
+                            p.tokens, p.heads, p.split, s);
+    if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;
+    ++launches;
+  }
+  g_last_launch_count = launches;
+  return DSA_STATUS_OK;
+}
+
+int dsa_merge_partials(const float* numerator, const float* partial_max, const float* partial_sum,
+                       void* output, float* softmax_max, float* softmax_sum, int64_t tokens,
+                       int64_t heads, int64_t split, void* stream) {
+  if (!numerator || !partial_max || !partial_sum || !output || !softmax_max || !softmax_sum)
+    return DSA_STATUS_BAD_ARGUMENT;
+  if (tokens <= 0 || heads <= 0 || split <= 0 || tokens * heads > 0x7fffffffLL)
+    return DSA_STATUS_BAD_ARGUMENT;
+  if (!aligned16(numerator) || (reinterpret_cast<uintptr_t>(output) & 7u) != 0)
+    return DSA_STATUS_BAD_ARGUMENT;
+  cudaError_t err = dsa::launch_merge(numerator, partial_max, partial_sum,
+                                      static_cast<__nv_bfloat16*>(output), softmax_max,
+                                      softmax_sum, (int)tokens, (int)heads, (int)split,
+                                      static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? DSA_STATUS_OK : DSA_STATUS_LAUNCH_FAILED;
+}
+
+int dsa_last_launch_count(void) { return g_last_launch_count; }
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+// Shared definitions for the sm_100a sparse-MLA forward kernels.
+//
+// Layout facts used everywhere (reference contract, dsa/api.py:23-43):
+//   q      [T, H, 512]  bf16, T = B*SQ flattened tokens (batch-major)
+//   q_rope [T, H, 64]   bf16
+//   kv     [B, L, 512]  bf16 (the size-1 head axis is dropped)
+//   k_rope [B, L, 64]   bf16
+//   ids    [T, TOPK]    int32
+//   out    [T, H, 512]  bf16; max/sum [T, H] fp32 (== [B,1,SQ,H] contiguous)
+//   split-KV partials (dsa/api.py:116-118): numerator [T, S, H, 512] fp32,
+//   partial max/sum [T, S, H] fp32.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsa {
+
+constexpr int kDimLatent = 512;
+constexpr int kDimRope = 64;
+constexpr int kDimQK = kDimLatent + kDimRope;  // 576
+constexpr float kNegFltMax = -3.4028234663852886e38f;
+
+// Device error bits OR-ed into the optional status word.
+constexpr int kErrTimeout = 1;
+constexpr int kErrBadLaunch = 2;
+
+struct FwdParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* kv;
+  const __nv_bfloat16* q_rope;
+  const __nv_bfloat16* k_rope;
+  const int32_t* ids;
+  __nv_bfloat16* out;     // split == 1
+  float* out_max;         // split == 1
+  float* out_sum;         // split == 1
+  float* part_num;        // split > 1: [T, S, H, 512]
+  float* part_max;        // split > 1: [T, S, H]
+  float* part_sum;        // split > 1: [T, S, H]
+  int32_t* status;
+  int batch, queries, heads, length, topk;
+  int tokens;             // batch * queries
+  int split;
+  int keys_per_tile;
+  int heads_per_cta;
+};
+
+// Split bounds in whole tiles, uneven when the tile count does not divide
+// (the tile-count split of dsa/ragged.py:141-143, generalised to a ragged
+// last tile): split s covers keys [begin, end).
+__host__ __device__ inline void split_bounds(int topk, int bn, int split, int s, int* begin,
+                                             int* end) {
+  int tiles = (topk + bn - 1) / bn;
+  int t0 = (int)(((long long)s * tiles) / split);
+  int t1 = (int)(((long long)(s + 1) * tiles) / split);
+  *begin = min(t0 * bn, topk);
+  *end = min(t1 * bn, topk);
+}
+
+// ---------------------------------------------------------------------------
+// Small PTX wrappers (warp-level MMA path).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                            uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                                  uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void report_error(int32_t* status, int bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+// Launchers (each returns a cudaError_t from the launch).
+cudaError_t launch_fwd_warp_mma(const FwdParams& p, cudaStream_t stream);
+cudaError_t launch_merge(const float* num, const float* pmax, const float* psum,
+                         __nv_bfloat16* out, float* omax, float* osum, int tokens, int heads,
+                         int split, cudaStream_t stream);
+
+}  // namespace dsa

@@ -1,0 +1,146 @@
+/*
+ * dsa_b200.h — C ABI of the B200 (sm_100a) sparse-MLA attention forward.
+ *
+ * This is the drop-in boundary for the one hot path of CHNJZ/dsa: the BF16
+ * sparse MLA forward with caller-given top-k indices,
+ *
+ *     forward(q, kv, q_rope, k_rope, indices) -> (output, softmax_max, softmax_sum)
+ *
+ * (reference: dsa/api.py:81-137). Shapes, dtypes and semantics are the
+ * reference's (dsa/api.py:23-43, dsa/api.py:82-91):
+ *
+ *   q        BF16  [B, SQ, H, 512]   contiguous
+ *   kv       BF16  [B, L, 1, 512]    contiguous (shared key and value)
+ *   q_rope   BF16  [B, SQ, H, 64]    contiguous
+ *   k_rope   BF16  [B, L, 1, 64]     contiguous
+ *   indices  INT32 [B, SQ, 1, TOPK]  contiguous; entries outside [0, L) are
+ *                                    masked (their address is clamped), and
+ *                                    duplicates keep their repeated weight
+ *   output       BF16 [B, SQ, H, 512]
+ *   softmax_max  FP32 [B, 1, SQ, H]  max_j s_j, with s_j = (q.kv_j + qr.kr_j)/24
+ *   softmax_sum  FP32 [B, 1, SQ, H]  sum_j exp(s_j - max)
+ *
+ * Every pointer is a device pointer on the current device. No function
+ * allocates device memory: temporaries (split-KV partials) live in a
+ * caller-provided workspace whose size dsa_fwd_workspace_bytes() reports.
+ * Launches are asynchronous on the given stream (a cudaStream_t passed as
+ * void*, NULL = legacy default stream); nothing synchronises the host.
+ *
+ * No torch types cross this boundary; the Python package binds it with
+ * ctypes (dsa_b200/_native.py).
+ */
+#ifndef DSA_B200_H_
+#define DSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSA_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DSA_B200_API __attribute__((visibility("default")))
+#else
+#define DSA_B200_API
+#endif
+
+/* Status codes. The Python wrapper maps BAD_ARGUMENT/UNSUPPORTED to
+ * ValueError and the rest to RuntimeError, as the reference raises
+ * ValueError for shape/config problems (dsa/api.py:27-42, 97). */
+typedef enum dsa_status {
+  DSA_STATUS_OK = 0,
+  DSA_STATUS_BAD_ARGUMENT = 1,      /* null pointer, non-positive size, misaligned buffer */
+  DSA_STATUS_UNSUPPORTED = 2,       /* launch entry not valid for this shape */
+  DSA_STATUS_WORKSPACE_TOO_SMALL = 3,
+  DSA_STATUS_LAUNCH_FAILED = 4,     /* cudaGetLastError() after a launch */
+  DSA_STATUS_DEVICE_TIMEOUT = 5,    /* a bounded device-side wait gave up (status word) */
+  DSA_STATUS_CUDA_ERROR = 6         /* other CUDA runtime error */
+} dsa_status_t;
+
+/* Kernel families of the sm_100a launch table (replaces the reference's
+ * workspace/ragged kernel choice, dsa/api.py:120-128). */
+typedef enum dsa_family {
+  DSA_FAMILY_AUTO = 0,      /* pick by shape (dsa_default_launch) */
+  DSA_FAMILY_WARP_MMA = 1,  /* generic: 16 heads per CTA, warp-level MMA, any H % 16 == 0 */
+  DSA_FAMILY_UMMA = 2       /* tcgen05/TMEM path: 2-CTA cluster, 128 heads per query */
+} dsa_family_t;
+
+/* One entry of the shape-keyed launch table (reference: Tuning,
+ * dsa/config.py:10-19, and its constraints dsa/api.py:46-65). */
+typedef struct dsa_launch {
+  int32_t family;          /* dsa_family_t */
+  int32_t heads_per_cta;   /* BM: heads sharing one gathered tile in one CTA */
+  int32_t keys_per_tile;   /* BN: gathered kv rows per pipeline stage */
+  int32_t split;           /* KV splits per (query, head tile); >1 writes FP32
+                              partials into the workspace, then merges */
+} dsa_launch_t;
+
+/* Arguments of one forward call (reference: forward's tensors and the
+ * kernel arguments of dsa/api.py:120-133). */
+typedef struct dsa_fwd_args {
+  const void* q;            /* BF16 [B,SQ,H,512] */
+  const void* kv;           /* BF16 [B,L,1,512] */
+  const void* q_rope;       /* BF16 [B,SQ,H,64] */
+  const void* k_rope;       /* BF16 [B,L,1,64] */
+  const int32_t* indices;   /* INT32 [B,SQ,1,TOPK] */
+  void* output;             /* BF16 [B,SQ,H,512] */
+  float* softmax_max;       /* FP32 [B,1,SQ,H] */
+  float* softmax_sum;       /* FP32 [B,1,SQ,H] */
+  int64_t batch, queries, heads, length, topk;
+  dsa_launch_t launch;      /* family AUTO => dsa_default_launch() */
+  void* workspace;          /* split-KV partials; may be NULL when the size is 0 */
+  uint64_t workspace_bytes;
+  int32_t* status;          /* optional device word; kernels only OR error bits
+                               into it (never clear it). NULL disables reporting. */
+} dsa_fwd_args_t;
+
+/* ABI version (DSA_B200_ABI_VERSION of the built library). No reference
+ * counterpart (the reference is JIT-compiled Python). */
+DSA_B200_API int dsa_abi_version(void);
+
+/* Human-readable name of a dsa_status_t. */
+DSA_B200_API const char* dsa_status_string(int status);
+
+/* Shape-keyed default launch entry (replaces the import-time validated
+ * table _DEFAULT_CONFIGS, dsa/api.py:68-78, and config.select,
+ * dsa/config.py:64-69). Depends only on the shape and the SM count of the
+ * current device, never on input values. Returns DSA_STATUS_OK. */
+DSA_B200_API int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t length,
+                       int64_t topk, dsa_launch_t* out);
+
+/* Check a launch entry against a shape (replaces _check_tuning,
+ * dsa/api.py:46-65). Returns OK or UNSUPPORTED. */
+DSA_B200_API int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t length,
+                     int64_t topk, const dsa_launch_t* launch);
+
+/* Workspace bytes the call needs (replaces the per-call torch.empty of the
+ * GM workspace and the split partials, dsa/api.py:107-118). Returns 0 for
+ * split == 1 and for an invalid entry. */
+DSA_B200_API uint64_t dsa_fwd_workspace_bytes(const dsa_fwd_args_t* args);
+
+/* The forward: main kernel and, when split > 1, the FP32 merge, both
+ * enqueued on `stream` (reference: forward, dsa/api.py:81-137).
+ * Returns a dsa_status_t. */
+DSA_B200_API int dsa_sparse_mla_fwd(const dsa_fwd_args_t* args, void* stream);
+
+/* Standalone FP32 split-KV merge (reference: merge_partials,
+ * dsa/merge.py:13-91): numerator FP32 [T,S,H,512] (unnormalised),
+ * partial_max/partial_sum FP32 [T,S,H] -> output BF16 [T,H,512],
+ * softmax_max/softmax_sum FP32 [T,H]. T = B*SQ tokens, S = splits. */
+DSA_B200_API int dsa_merge_partials(const float* numerator, const float* partial_max,
+                       const float* partial_sum, void* output, float* softmax_max,
+                       float* softmax_sum, int64_t tokens, int64_t heads, int64_t split,
+                       void* stream);
+
+/* Number of kernels the last successful dsa_sparse_mla_fwd on this host
+ * thread enqueued (1 or 2), for launch accounting. */
+DSA_B200_API int dsa_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_B200_H_ */

@@ -1,0 +1,145 @@
+"""The CPU oracle against the reference's known answers and recorded pins.
+
+Known answers: DSA从原理到实现.md:159-219 (online softmax by hand, split
+merge, naive averaging is wrong) and :104 (duplicates keep weight).
+Pins: tests/golden/reference_pins.json, the reference's own oracle figures
+(reference_max, ref_sq) from validation/*/result.json for seeded inputs.
+"""
+import json
+import math
+import os
+
+import pytest
+import torch
+
+from oracle import sparse_mla as oracle
+
+PINS = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_pins.json")))
+
+
+def test_online_softmax_hand_example():
+    scores, values = [1.0, 2.0, 3.0], [10.0, 20.0, 40.0]
+    m_a, l_a, u_a = oracle.online_softmax(scores, values, [(0, 2)])
+    assert m_a == 2.0
+    assert l_a == pytest.approx(1.367879441, abs=1e-9)
+    assert u_a == pytest.approx(23.678794412, abs=1e-9)
+    m, l, u = oracle.online_softmax(scores, values, [(0, 2), (2, 3)])
+    assert l == pytest.approx(1.503214724, abs=1e-9)
+    assert u == pytest.approx(48.710941656, abs=1e-9)
+    assert u / l == pytest.approx(32.40451338379263, abs=1e-12)
+
+
+def test_split_merge_hand_example():
+    num = torch.tensor([[[[23.678794412]], [[40.0]]]], dtype=torch.float64)  # [T=1,S=2,H=1,1]
+    pm = torch.tensor([[[2.0], [3.0]]], dtype=torch.float64)
+    pl = torch.tensor([[[1.367879441], [1.0]]], dtype=torch.float64)
+    out, m, l = oracle.merge_partials(num, pm, pl)
+    assert float(out) == pytest.approx(32.404513384, abs=1e-8)
+    naive = (23.678794412 / 1.367879441 + 40.0) / 2
+    assert naive == pytest.approx(28.655292893, abs=1e-8)
+    assert abs(naive - float(out)) > 1.0
+
+
+def test_duplicates_keep_weight():
+    shape = (1, 1, 16, 64, 3)
+    q, kv, qr, kr, _ = oracle.make_inputs(shape, 7, "normal")
+    dup = torch.tensor([5, 5, 9], dtype=torch.int32).reshape(1, 1, 1, 3)
+    uniq = torch.tensor([5, 9, -1], dtype=torch.int32).reshape(1, 1, 1, 3)
+    o_dup = oracle.reference_forward(q, kv, qr, kr, dup)[0]
+    o_uniq = oracle.reference_forward(q, kv, qr, kr, uniq)[0]
+    assert not torch.allclose(o_dup, o_uniq, atol=1e-4)
+
+
+def test_invalid_indices_are_masked():
+    shape = (1, 2, 16, 64, 8)
+    q, kv, qr, kr, ids = oracle.make_inputs(shape, 11, "normal")
+    bad = ids.clone()
+    bad[..., 4:] = torch.tensor([-1, 64, 1000, -7], dtype=torch.int32)
+    trimmed = oracle.reference_forward(q, kv, qr, kr, bad)
+    only = oracle.reference_forward(q, kv, qr, kr, ids[..., :4].contiguous())
+    for a, b in zip(trimmed, only):
+        torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6)
+
+
+def test_merge_matches_unsplit():
+    shape = (1, 3, 16, 512, 96)
+    q, kv, qr, kr, ids = oracle.make_inputs(shape, 3, "peaked")
+    full = oracle.reference_forward(q, kv, qr, kr, ids)
+    parts = []
+    for lo, hi in ((0, 40), (40, 41), (41, 96)):
+        sub = ids[..., lo:hi].contiguous()
+        o, m, l = oracle.reference_forward(q, kv, qr, kr, sub)
+        parts.append((o * l[:, 0, :, :, None], m[:, 0], l[:, 0]))
+    num = torch.stack([p[0].reshape(3, 16, 512) for p in parts], 1)
+    pm = torch.stack([p[1].reshape(3, 16) for p in parts], 1)
+    pl = torch.stack([p[2].reshape(3, 16) for p in parts], 1)
+    out, m, l = oracle.merge_partials(num, pm, pl)
+    torch.testing.assert_close(out, full[0].reshape(3, 16, 512), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(m, full[1].reshape(3, 16), rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(l, full[2].reshape(3, 16), rtol=1e-5, atol=1e-6)
+
+
+def test_query_range_matches_full():
+    shape = (2, 5, 16, 256, 32)
+    data = oracle.make_inputs(shape, 5, "normal")
+    full = oracle.reference_forward(*data)
+    part = oracle.reference_forward(*data, query_range=(3, 9))
+    flat = full[0].reshape(10, 16, 512)
+    torch.testing.assert_close(part[0], flat[3:9])
+    torch.testing.assert_close(part[1], full[1].reshape(10, 16)[3:9])
+
+
+def _pin_id(pin):
+    return f"{pin['case']}-{pin['family']}-{pin['seed']}"
+
+
+FAST_PINS = [p for p in PINS if not p["case"].startswith("prefill_b4")]
+SLOW_PINS = [p for p in PINS if p["case"].startswith("prefill_b4")]
+
+
+@pytest.mark.parametrize("pin", FAST_PINS, ids=_pin_id)
+def test_reference_pins(pin):
+    """make_inputs + reference_forward reproduce the reference's recorded
+    oracle figures (NPU FP32 vs CPU FP32: agreement to ~1e-6 relative)."""
+    data = oracle.make_inputs(tuple(pin["shape"]), pin["seed"], pin["family"])
+    got = oracle.reference_forward(*data)
+    for key, tensor in zip(("output", "maximum", "denominator"), got):
+        want = pin["stats"][key]
+        assert tensor.numel() == want["elements"]
+        ref_max = float(tensor.abs().max())
+        ref_sq = float(tensor.double().square().sum())
+        assert ref_max == pytest.approx(want["reference_max"], rel=1e-5), key
+        assert ref_sq == pytest.approx(want["ref_sq"], rel=1e-5), key
+
+
+@pytest.mark.slow
+@pytest.mark.skipif(os.environ.get("DSA_SLOW_TESTS") != "1", reason="set DSA_SLOW_TESTS=1 (tens of GB of RAM)")
+@pytest.mark.parametrize("pin", SLOW_PINS, ids=_pin_id)
+def test_reference_pins_prefill_b4(pin):
+    test_reference_pins(pin)
+
+
+def test_baseline_index_variants():
+    b, s, length, k = 2, 1, 65536, 2048
+    uni = oracle.make_indices_variant(b, s, length, k, 1, "uniform")
+    peak = oracle.make_indices_variant(b, s, length, k, 1, "peaked")
+    dup = oracle.make_indices_variant(b, s, length, k, 1, "duplicates")
+    for ids in (uni, peak, dup):
+        assert ids.shape == (b, s, 1, k) and ids.dtype == torch.int32
+        assert int(ids.min()) >= 0 and int(ids.max()) < length
+    for row in uni.reshape(-1, k):
+        assert row.unique().numel() == k
+    for row in peak.reshape(-1, k):
+        assert row.unique().numel() == k
+        assert int((row >= length - 4096).sum()) == round(0.7 * k)
+    for row in dup.reshape(-1, k):
+        assert row.unique().numel() == k - round(0.1 * k)
+
+
+def test_accuracy_metric_definition():
+    e = torch.tensor([[1.0, -2.0], [0.5, 0.25]])
+    a = e + torch.tensor([[0.1, 0.0], [0.0, -0.05]])
+    m = oracle.accuracy([a, a, a], [e, e, e])["output"]
+    assert m["max_normalized"] == pytest.approx(0.1 / 2.0)
+    assert m["max_row_normalized"] == pytest.approx(max(0.1 / 2.0, 0.05 / 0.5))
+    assert math.isfinite(m["relative_rms"])
