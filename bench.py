@@ -51,7 +51,11 @@ DEFAULT_CONFIG = "prefill_h128"
 # Dominant-kernel DRAM traffic per launch (dram__bytes_read.sum +
 # dram__bytes_write.sum) from the ncu captures summarised under profiles/;
 # None until a capture of that kernel/config exists.
-TRAFFIC_BYTES = {}
+TRAFFIC_BYTES = {
+    # profiles/fwd_warp_mma_prefill_h128.md: 470.6 MB for a 512-query capture,
+    # scaled to 16384 queries.
+    "prefill_h128": int(470.6e6 * 16384 / 512),
+}
 
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
@@ -300,6 +304,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
+    ap.add_argument("--shape", default=None,
+                    help="B,SQ,H,L,TOPK override (a reduced case for profiling; workload 'custom')")
     ap.add_argument("--variant", default="uniform", choices=("uniform", "peaked", "duplicates"))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--e2e-steps", type=int, default=None)
@@ -309,6 +315,11 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     shape = CONFIGS[args.config]
+    if args.shape:
+        shape = tuple(int(v) for v in args.shape.split(","))
+        if len(shape) != 5:
+            raise SystemExit("--shape needs B,SQ,H,L,TOPK")
+        args.config = "custom"
     if args.impl == "reference":
         return run_reference(args, shape)
 
