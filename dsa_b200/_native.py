@@ -35,7 +35,12 @@ EXPORTS = (
     "dsa_sparse_mla_fwd",
     "dsa_merge_partials",
     "dsa_last_launch_count",
+    "dsa_sparse_mla_fwd_noalloc",
 )
+
+# Byte size of the built-in scratch array of dsa_sparse_mla_fwd_noalloc
+# (DSA_NOALLOC_SCRATCH_BYTES in include/dsa_b200.h).
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 
 class Launch(ctypes.Structure):
@@ -87,6 +92,8 @@ def load():
         lib.dsa_merge_partials.restype = ctypes.c_int
         lib.dsa_merge_partials.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
         lib.dsa_last_launch_count.restype = ctypes.c_int
+        lib.dsa_sparse_mla_fwd_noalloc.restype = ctypes.c_int
+        lib.dsa_sparse_mla_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
         version = lib.dsa_abi_version()
         if version != ABI_VERSION:
             raise RuntimeError(f"libdsa_b200.so ABI {version} != expected {ABI_VERSION}; rebuild it")

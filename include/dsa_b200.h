@@ -139,6 +139,26 @@ DSA_B200_API int dsa_merge_partials(const float* numerator, const float* partial
  * thread enqueued (1 or 2), for launch accounting. */
 DSA_B200_API int dsa_last_launch_count(void);
 
+/* Size of the library's built-in scratch array used by
+ * dsa_sparse_mla_fwd_noalloc (32 MiB, held on every GPU that loads the
+ * library until the process exits). */
+#define DSA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* Forward that allocates nothing and takes no workspace: the same warp-MMA
+ * split-KV kernels and FP32 merge as dsa_sparse_mla_fwd, with the split
+ * partials kept in the library's own DSA_NOALLOC_SCRATCH_BYTES array.
+ * It has no counterpart in the reference. It is for callers that cannot
+ * call cudaMalloc on this path: engines whose memory pool already holds
+ * the HBM, code that must not pay cudaFree's device-wide synchronisation,
+ * and FFI hosts that own only the input and output buffers. args->workspace
+ * is ignored; launch family must be AUTO or WARP_MMA. Returns
+ * DSA_STATUS_WORKSPACE_TOO_SMALL when the partials (tokens * split * heads
+ * * 2056 bytes, 256-byte aligned per region) exceed the array. The first
+ * call on a device resolves the array's device address (make it before any
+ * stream capture). All calls share the array: calls that overlap on the GPU
+ * race with each other. */
+DSA_B200_API int dsa_sparse_mla_fwd_noalloc(const dsa_fwd_args_t* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
