@@ -73,7 +73,10 @@ def _check_tuning(config, shape, cores):
 
 
 def _launch_from_tuning(config, shape):
-    launch = _native.Launch(_native.FAMILY_WARP_MMA, 16, config.bn, config.split)
+    if config.bm == 128:
+        launch = _native.Launch(_native.FAMILY_UMMA, 128, config.bn, config.split)
+    else:
+        launch = _native.Launch(_native.FAMILY_WARP_MMA, 16, config.bn, config.split)
     code = _native.load().dsa_check_launch(*shape, ctypes.byref(launch))
     if code != _native.STATUS_OK:
         raise ValueError(f"Tuning {config} is not supported on sm_100a for shape {shape}: "

@@ -84,6 +84,10 @@ int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t leng
       if (bn != 32 && bn != 64) return DSA_STATUS_UNSUPPORTED;
       break;
     }
+    case DSA_FAMILY_UMMA: {
+      if (launch->heads_per_cta != 128 || heads != 128 || bn != 32) return DSA_STATUS_UNSUPPORTED;
+      break;
+    }
     default:
       return DSA_STATUS_UNSUPPORTED;
   }
@@ -98,6 +102,23 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
     return DSA_STATUS_BAD_ARGUMENT;
   if (heads % 16 != 0) return DSA_STATUS_UNSUPPORTED;
   dsa_launch_t e;
+  if (heads == 128) {
+    // tcgen05 family: persistent CTAs over (token, split, V half) items;
+    // split the TOPK range only until every resident CTA has an item.
+    e.family = DSA_FAMILY_UMMA;
+    e.heads_per_cta = 128;
+    e.keys_per_tile = 32;
+    int ctas = dsa::umma_max_ctas();
+    if (ctas <= 0) ctas = sm_count();
+    const int64_t halves = 2 * batch * queries;
+    const int64_t tiles = (topk + 31) / 32;
+    int64_t split = (ctas + halves - 1) / halves;
+    if (split > tiles) split = tiles;
+    if (split < 1) split = 1;
+    e.split = (int32_t)split;
+    *out = e;
+    return DSA_STATUS_OK;
+  }
   e.family = DSA_FAMILY_WARP_MMA;
   e.heads_per_cta = 16;
   e.keys_per_tile = 32;
@@ -185,6 +206,7 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
   cudaError_t err = cudaSuccess;
   switch (e.family) {
     case DSA_FAMILY_WARP_MMA: err = dsa::launch_fwd_warp_mma(p, s); break;
+    case DSA_FAMILY_UMMA: err = dsa::launch_fwd_umma(p, s); break;
     default: return DSA_STATUS_UNSUPPORTED;
   }
   if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;

@@ -1,0 +1,469 @@
+// tcgen05/TMEM sparse-MLA forward for H = 128 heads (the "umma" family).
+//
+// Work item = (token, KV split, V half r). A persistent CTA (one per SM)
+// loops over items; the two halves of a (token, split) are consecutive items,
+// so they run at the same time on neighbouring SMs and the second gather of
+// each row hits L2. Per item and per tile of 32 selected rows:
+//
+//   S    = Q . K^T                          (tcgen05, M=128 heads, N=32 keys, K=576)
+//   P    = bf16(exp(S/24 - m))              (FP32 online softmax, thread = head row)
+//   O_r += P . V[:, 256r .. 256r+256)       (tcgen05, M=128, N=256, K=32 keys)
+//
+// Both halves compute the full S (1.53x the minimum MMA work) so that no
+// data crosses SMs: O for 128 heads x 512 dims needs all 512 TMEM columns of
+// one SM, and exchanging partial scores between SMs every tile costs more
+// than the duplicated QK.
+//
+// TMEM (512 columns): O_r [0, 256), two S buffers [256, 320), Q latent dims
+// 0..383 as BF16 pairs [320, 512) — the A operand of 24 of the 36 QK MMA
+// steps. Q dims 384..511 and the 64 rope dims sit in shared memory (128-byte
+// swizzle), as do the gathered rows (4 stages x 32 rows x 1152 B) and P.
+//
+// Warp roles (9 warps): warps 0-3 gather (warp w owns stage w: 16-byte
+// cp.async of the indexed rows into swizzled K-major tiles plus a validity
+// bitmask); warp 4 (one lane) issues the MMAs; warps 5-8 run the softmax, one
+// head row per thread, load Q per item and write the output. The online
+// softmax keeps the reference's semantics (dsa/workspace.py:242-318):
+// invalid index -> -inf, FP32 max/sum, BF16 P, FP32 O. O is only rescaled
+// when the row max grows by more than 2^8 in exp2 units (lazy rescale); the
+// reported max is the true max and the sum is rescaled to it at the end.
+//
+// No TMA and no clusters are used. Every wait is bounded and reports through
+// the status word.
+#include "umma_ptx.cuh"
+
+namespace dsa {
+namespace {
+
+using namespace umma;
+
+constexpr int kUmBN = 32;          // keys per tile
+constexpr int kUmStages = 4;       // gather pipeline depth (one gather warp per stage)
+constexpr int kGatherWarps = kUmStages;
+constexpr int kMmaWarp = kGatherWarps;          // 4
+constexpr int kSoftWarp0 = kMmaWarp + 1;        // 5
+constexpr int kSoftWarps = 4;
+constexpr int kUmThreads = 32 * (kSoftWarp0 + kSoftWarps);  // 288
+constexpr int kUmHeads = 128;
+constexpr int kQTmemDims = 384;    // Q latent dims kept in TMEM
+
+// Shared-memory layout (bytes from a 1024-aligned base).
+constexpr uint32_t kQBlock = 128u * 128u;                    // 128 heads x 64 dims (SW128)
+constexpr uint32_t kOffQ = 0;                                // Q dims 384..511 (2 blocks) + rope (1 block)
+constexpr uint32_t kQBytes = 3u * kQBlock;                   // 49152
+constexpr uint32_t kKBlock = (uint32_t)kUmBN * 128u;         // 4096: 32 keys x 64 dims (SW128)
+constexpr uint32_t kKStage = 9u * kKBlock;                   // 8 latent blocks + 1 rope block
+constexpr uint32_t kOffK = kOffQ + kQBytes;
+constexpr uint32_t kOffP = kOffK + kUmStages * kKStage;      // P: 128 rows x 32 keys (SW64)
+constexpr uint32_t kPBytes = 128u * (uint32_t)kUmBN * 2u;    // 8192
+constexpr uint32_t kOffMask = kOffP + kPBytes;               // validity bits per stage
+constexpr uint32_t kOffBar = kOffMask + 64u;
+
+enum Bar {
+  kFull0 = 0,
+  kEmpty0 = kFull0 + kUmStages,
+  kQFull = kEmpty0 + kUmStages,
+  kSFull0,
+  kSFree0 = kSFull0 + 2,
+  kPFull = kSFree0 + 2,
+  kPvDone,
+  kBarCount
+};
+constexpr uint32_t kOffTmemSlot = kOffBar + kBarCount * 8u;
+constexpr uint32_t kOffAbort = kOffTmemSlot + 8u;
+constexpr uint32_t kSmemUsed = kOffAbort + 8u;
+constexpr uint32_t kSmemBytes = kSmemUsed + 1024u;  // slack for the 1024-byte alignment
+
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = 0;
+constexpr uint32_t kTmemS = 256;
+constexpr uint32_t kTmemQ = 320;
+
+static_assert(kOffK % 1024 == 0 && kKStage % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms");
+static_assert(kTmemQ + kQTmemDims / 2 == kTmemCols, "TMEM budget");
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+struct Item {
+  int token, sp, half, batch, kbeg, kend, ntiles;
+};
+
+__device__ __forceinline__ Item make_item(const FwdParams& p, int item) {
+  Item it;
+  it.half = item & 1;
+  const int ts = item >> 1;
+  it.token = ts / p.split;
+  it.sp = ts % p.split;
+  it.batch = it.token / p.queries;
+  split_bounds(p.topk, kUmBN, p.split, it.sp, &it.kbeg, &it.kend);
+  it.ntiles = (it.kend - it.kbeg + kUmBN - 1) / kUmBN;
+  return it;
+}
+
+__device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(v); }
+__device__ __forceinline__ uint32_t f2u(float v) { return __float_as_uint(v); }
+
+// 2^x on the special-function unit (flushes results below 2^-126 to zero,
+// far below what the FP32 row sums can resolve).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Bounded wait whose result is the same in every lane of the warp.
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+__global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const sbase = smem_raw + (base - raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sbase + kOffAbort);
+  auto bar = [&](int i) -> uint32_t { return base + kOffBar + 8u * (uint32_t)i; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kUmStages; ++s) {
+      mbar_init(bar(kFull0 + s), 1);
+      mbar_init(bar(kEmpty0 + s), 1);
+    }
+    mbar_init(bar(kQFull), kSoftWarps);
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(bar(kSFull0 + k), 1);
+      mbar_init(bar(kSFree0 + k), kSoftWarps);
+    }
+    mbar_init(bar(kPFull), kSoftWarps);
+    mbar_init(bar(kPvDone), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(base + kOffTmemSlot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sbase + kOffTmemSlot);
+
+  const int n_items = p.tokens * p.split * 2;
+  const int L = p.length;
+
+  if (warp < kGatherWarps) {
+    // ---------------- gather: warp w fills stage w for tiles g = w, w+4, ... ----------------
+    const uint32_t s = (uint32_t)warp;
+    const uint32_t stage = base + kOffK + s * kKStage;
+    uint32_t* const mask_s = reinterpret_cast<uint32_t*>(sbase + kOffMask) + s;
+    uint32_t g = 0, n = 0;  // g: tile counter of this CTA, n: tiles this warp filled
+    bool ok = true;
+    // lane -> (key quarter kq, 16-byte chunk j8): 4 rows x 128 contiguous bytes per instruction
+    const int j8 = lane & 7;
+    const int kq = lane >> 3;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const Item w = make_item(p, item);
+      const int32_t* ids_t = p.ids + (size_t)w.token * p.topk;
+      const __nv_bfloat16* const kv_b = p.kv + (size_t)w.batch * L * kDimLatent;
+      const __nv_bfloat16* const kr_b = p.k_rope + (size_t)w.batch * L * kDimRope;
+      for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
+        if (g % kUmStages != s) continue;
+        if (n > 0) {  // the stage's previous tile (g - 4) has been consumed by its PV
+          if (lane == 0) ok = mbar_wait(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag);
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+        }
+        const int j = w.kbeg + t * kUmBN + lane;
+        const int idx = j < w.kend ? __ldg(ids_t + j) : -1;
+        const int row = min(max(idx, 0), L - 1);  // clamped address; masked below
+        const uint32_t bits = __ballot_sync(0xffffffffu, (idx >= 0) & (idx < L));
+        if (lane == 0) *mask_s = bits;
+#pragma unroll 2
+        for (int i = 0; i < kUmBN / 4; ++i) {
+          const int k = kq + 4 * i;
+          const int rk = __shfl_sync(0xffffffffu, row, k);
+          const uint32_t dst = stage + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u +
+                               (uint32_t)((j8 ^ (k & 7)) * 16);
+          const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
+#pragma unroll
+          for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * kKBlock, src + kb * 64);
+          cp_async_16(dst + 8 * kKBlock, kr_b + (size_t)rk * kDimRope + j8 * 8);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kFull0 + s));
+        ++n;
+      }
+    }
+    if (!ok) report_error(p.status, kErrTimeout);
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer (one lane) ----------------
+    if (lane == 0) {
+      const uint32_t idesc_qk = idesc_bf16(128, kUmBN, false, false);
+      const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
+      uint32_t g = 0, it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+        const Item w = make_item(p, item);
+        const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
+        auto issue_pv = [&](uint32_t gp, bool first) -> bool {
+          if (!mbar_wait(bar(kPFull), gp & 1u, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t stage = base + kOffK + (gp % kUmStages) * kKStage;
+#pragma unroll
+          for (int j = 0; j < kUmBN / 16; ++j) {
+            const uint64_t ad = smem_desc(base + kOffP + j * 32, 16, 512, kLayoutSw64);
+            const uint64_t bd = smem_desc(stage + vblk + j * 2048, kKBlock, 1024, kLayoutSw128);
+            mma_bf16_ss(tmem + kTmemO, ad, bd, idesc_pv, (first && j == 0) ? 0u : 1u);
+          }
+          mma_commit(bar(kPvDone));
+          mma_commit(bar(kEmpty0 + gp % kUmStages));
+          return true;
+        };
+        ok = mbar_wait(bar(kQFull), it & 1u, abort_flag);
+        tc_fence_after();
+        for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
+          const uint32_t s = g % kUmStages;
+          const uint32_t b = g & 1u;
+          ok = mbar_wait(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
+          if (ok && g >= 2) ok = mbar_wait(bar(kSFree0 + b), ((g - 2) >> 1) & 1u, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t stage = base + kOffK + s * kKStage;
+          const uint32_t d = tmem + kTmemS + b * kUmBN;
+#pragma unroll
+          for (int ks = 0; ks < kQTmemDims / 16; ++ks) {  // dims 0..383: A = Q from TMEM
+            const uint64_t bd =
+                smem_desc(stage + (ks >> 2) * kKBlock + (uint32_t)(ks & 3) * 32u, 16, 1024, kLayoutSw128);
+            mma_bf16_ts(d, tmem + kTmemQ + (uint32_t)ks * 8u, bd, idesc_qk, ks > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int ks = kQTmemDims / 16; ks < kDimQK / 16; ++ks) {  // dims 384..575: A from smem
+            const uint32_t qb = (uint32_t)(ks - kQTmemDims / 16) >> 2;
+            const uint64_t ad = smem_desc(base + kOffQ + qb * kQBlock + (uint32_t)(ks & 3) * 32u, 16, 1024,
+                                          kLayoutSw128);
+            const uint64_t bd =
+                smem_desc(stage + (ks >> 2) * kKBlock + (uint32_t)(ks & 3) * 32u, 16, 1024, kLayoutSw128);
+            mma_bf16_ss(d, ad, bd, idesc_qk, 1u);
+          }
+          mma_commit(bar(kSFull0 + b));
+          if (t > 0) ok = issue_pv(g - 1, t == 1);
+        }
+        if (ok) ok = issue_pv(g - 1, w.ntiles == 1);
+      }
+      if (!ok) report_error(p.status, kErrTimeout);
+    }
+  } else {
+    // ---------------- softmax + epilogue (one head row per thread) ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant of this warp
+    const int row = quad * 32 + lane;
+    const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
+    const float c = 1.4426950408889634f / 24.0f;  // log2(e) / 24
+    uint8_t* const prow = sbase + kOffP + (uint32_t)(row >> 3) * 512u + (uint32_t)(row & 7) * 64u;
+    const uint32_t* const mask_all = reinterpret_cast<const uint32_t*>(sbase + kOffMask);
+    uint32_t g = 0, it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+      const Item w = make_item(p, item);
+      // Q of this head row: dims 0..383 -> TMEM, dims 384..511 and the rope
+      // dims -> shared memory (128-byte swizzle). The previous item's MMAs are
+      // complete (its epilogue waited for its last PV).
+      {
+        const size_t qrow = (size_t)w.token * kUmHeads + row;
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
+#pragma unroll 1
+        for (int ch = 0; ch < kQTmemDims / 64; ++ch) {
+          uint32_t r[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 v = __ldg(src + ch * 8 + i);
+            r[4 * i] = v.x;
+            r[4 * i + 1] = v.y;
+            r[4 * i + 2] = v.z;
+            r[4 * i + 3] = v.w;
+          }
+          tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
+        }
+        uint8_t* const qdst = sbase + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)  // latent dims 384..511: 2 blocks x 8 chunks
+          *reinterpret_cast<uint4*>(qdst + (i >> 3) * kQBlock + (((i & 7) ^ (row & 7)) * 16)) =
+              __ldg(src + kQTmemDims / 8 + i);
+        const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<uint4*>(qdst + 2 * kQBlock + ((i ^ (row & 7)) * 16)) = __ldg(rsrc + i);
+        fence_proxy_async_smem();
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kQFull));
+      }
+      float m_true = kNegFltMax, m_used = kNegFltMax, l = 0.f;
+      for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
+        const uint32_t s = g % kUmStages;
+        const uint32_t b = g & 1u;
+        ok = wait_warp(bar(kSFull0 + b), (g >> 1) & 1u, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        float x[32];
+        {
+          uint32_t sv[32];
+          tmem_ld32(tmem + t_lane + kTmemS + b * kUmBN, sv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = u2f(sv[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kSFree0 + b));
+        // validity bits of the tile's keys (written by the gather warp)
+        ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
+        if (!ok) break;
+        const uint32_t mbits = mask_all[s];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          x[k] = ((mbits >> k) & 1u) ? x[k] : -INFINITY;
+          mx = fmaxf(mx, x[k]);
+        }
+        m_true = fmaxf(m_true, mx);
+        float alpha = 1.f;
+        bool resc = false;
+        if ((mx - m_used) * c > 8.f) {
+          alpha = ex2((m_used - mx) * c);
+          m_used = mx;
+          resc = true;
+        }
+        const float mc = m_used * c;
+        float sum = 0.f;
+        uint32_t packed[16];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const float p0 = ex2(fmaf(x[k], c, -mc));
+          const float p1 = ex2(fmaf(x[k + 1], c, -mc));
+          sum += p0 + p1;
+          packed[k / 2] = pack_bf16x2(p0, p1);
+        }
+        l = l * alpha + sum;
+        // P (single buffer) is free once the previous PV finished reading it
+        if (g >= 1) ok = wait_warp(bar(kPvDone), (g - 1) & 1u, abort_flag);
+        if (!ok) break;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(prow + ((q ^ ((row & 7) >> 1)) * 16)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        fence_proxy_async_smem();
+        if (__any_sync(0xffffffffu, resc) && t > 0) {
+          tc_fence_after();
+          uint32_t o[32];
+#pragma unroll 1
+          for (int cb = 0; cb < 256; cb += 32) {
+            const uint32_t a = tmem + t_lane + kTmemO + cb;
+            tmem_ld32(a, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
+            tmem_st32(a, o);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kPFull));
+      }
+      if (!ok) break;
+      // ---- epilogue: this CTA's 256 dims of the head row -> output (or FP32 partial) ----
+      ok = wait_warp(bar(kPvDone), (g - 1) & 1u, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const float f = (m_true == kNegFltMax) ? 1.f : ex2((m_used - m_true) * c);
+      const size_t orow = (size_t)w.token * kUmHeads + row;
+      const int col0 = w.half * 256;
+      if (p.split == 1) {
+        __nv_bfloat16* dst = p.out + orow * kDimLatent + col0;
+#pragma unroll 1
+        for (int cb = 0; cb < 256; cb += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem + t_lane + kTmemO + cb, o);
+          tmem_wait_ld();
+          uint32_t h[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            h[i] = pack_bf16x2(__fdiv_rn(u2f(o[2 * i]), l), __fdiv_rn(u2f(o[2 * i + 1]), l));
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+        }
+        if (w.half == 0) {
+          p.out_max[orow] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, 24.0f);
+          p.out_sum[orow] = l * f;
+        }
+      } else {
+        const size_t prow_idx = ((size_t)w.token * p.split + w.sp) * kUmHeads + row;
+        float* dst = p.part_num + prow_idx * kDimLatent + col0;
+#pragma unroll 1
+        for (int cb = 0; cb < 256; cb += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem + t_lane + kTmemO + cb, o);
+          tmem_wait_ld();
+          float4* d4 = reinterpret_cast<float4*>(dst + cb);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(u2f(o[4 * i]) * f, u2f(o[4 * i + 1]) * f, u2f(o[4 * i + 2]) * f,
+                                u2f(o[4 * i + 3]) * f);
+        }
+        if (w.half == 0) {
+          p.part_max[prow_idx] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, 24.0f);
+          p.part_sum[prow_idx] = l * f;
+        }
+      }
+      tc_fence_before();
+    }
+    if (!ok) report_error(p.status, kErrTimeout);
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+int umma_max_ctas() {
+  static int cached = -1;
+  if (cached > 0) return cached;
+  if (cudaFuncSetAttribute(fwd_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes) != cudaSuccess)
+    return -1;
+  int per_sm = 0, dev = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_umma_kernel, kUmThreads, kSmemBytes) !=
+          cudaSuccess ||
+      per_sm <= 0)
+    return -1;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return -1;
+  cached = per_sm * sms;
+  return cached;
+}
+
+cudaError_t launch_fwd_umma(const FwdParams& p, cudaStream_t stream) {
+  if (p.heads != kUmHeads || p.keys_per_tile != kUmBN) return cudaErrorInvalidValue;
+  const int max_ctas = umma_max_ctas();
+  if (max_ctas <= 0) return cudaErrorInvalidConfiguration;
+  const long long items = (long long)p.tokens * p.split * 2;
+  const int ctas = (int)(items < max_ctas ? items : max_ctas);
+  fwd_umma_kernel<<<ctas, kUmThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace dsa
