@@ -52,9 +52,9 @@ DEFAULT_CONFIG = "prefill_h128"
 # dram__bytes_write.sum) from the ncu captures summarised under profiles/;
 # None until a capture of that kernel/config exists.
 TRAFFIC_BYTES = {
-    # profiles/fwd_warp_mma_prefill_h128.md: 470.6 MB for a 512-query capture,
-    # scaled to 16384 queries.
-    "prefill_h128": int(470.6e6 * 16384 / 512),
+    # profiles/fwd_umma_prefill_h128.md: 398.6 MB for a 512-query capture of
+    # fwd_umma_kernel, scaled to 16384 queries.
+    "prefill_h128": int(398.6e6 * 16384 / 512),
 }
 
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
@@ -164,7 +164,7 @@ def compact_for_oracle(data, rows):
 # Clock sampling during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -194,7 +194,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, start, end):
+        """Host wall-clock bounds of the timed region."""
+        self.window = (start, end)
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -209,7 +213,10 @@ class ClockSampler:
     def summary(self):
         sms, maxes, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
+        lo, hi = getattr(self, "window", (0.0, float("inf")))
+        for stamp, line in self.lines:
+            if not (lo - 0.05 <= stamp <= hi + 0.25):  # output lags the sample slightly
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -358,6 +365,8 @@ def main():
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches_total = 0
     with ClockSampler(local) as clocks:
+        time.sleep(0.3)  # let nvidia-smi start sampling before the timed region
+        t_host0 = time.time()
         for i in range(args.steps):
             flush.fill_(float(i))  # evict L2 between timed iterations (outside the events)
             starts[i].record(stream)
@@ -365,6 +374,7 @@ def main():
             ends[i].record(stream)
             launches_total += n
         torch.cuda.synchronize()
+        clocks.mark(t_host0, time.time())
     durations = [a.elapsed_time(e) for a, e in zip(starts, ends)]  # ms
     total_ms = sum(durations)
     if world > 1:

@@ -9,24 +9,29 @@
 //   P    = bf16(exp(S/24 - m))              (FP32 online softmax, thread = head row)
 //   O_r += P . V[:, 256r .. 256r+256)       (tcgen05, M=128, N=256, K=32 keys)
 //
-// Both halves compute the full S (1.53x the minimum MMA work) so that no
-// data crosses SMs: O for 128 heads x 512 dims needs all 512 TMEM columns of
-// one SM, and exchanging partial scores between SMs every tile costs more
-// than the duplicated QK.
+// Both halves compute the full S (1.53x the minimum MMA work) so that no data
+// crosses SMs: O for 128 heads x 512 dims needs all 512 TMEM columns of one
+// SM, and exchanging partial scores between SMs every tile costs more than
+// the duplicated QK.
 //
-// TMEM (512 columns): O_r [0, 256), two S buffers [256, 320), Q latent dims
-// 0..383 as BF16 pairs [320, 512) — the A operand of 24 of the 36 QK MMA
-// steps. Q dims 384..511 and the 64 rope dims sit in shared memory (128-byte
-// swizzle), as do the gathered rows (4 stages x 32 rows x 1152 B) and P.
+// A tcgen05.mma costs its issuing warp ~120 cycles whatever its size, so the
+// narrow (N = 32) QK MMAs are spread over three issuer warps, each with its
+// own S accumulator (tile g -> issuer and S buffer g mod 3), and the PV MMAs
+// have a fourth issuer. The A operand of 20 of the 36 QK steps (Q dims
+// 0..319) is read from TMEM, so those steps cost no shared-memory bandwidth.
 //
-// Warp roles (9 warps): warps 0-3 gather (warp w owns stage w: 16-byte
-// cp.async of the indexed rows into swizzled K-major tiles plus a validity
-// bitmask); warp 4 (one lane) issues the MMAs; warps 5-8 run the softmax, one
-// head row per thread, load Q per item and write the output. The online
-// softmax keeps the reference's semantics (dsa/workspace.py:242-318):
-// invalid index -> -inf, FP32 max/sum, BF16 P, FP32 O. O is only rescaled
-// when the row max grows by more than 2^8 in exp2 units (lazy rescale); the
-// reported max is the true max and the sum is rescaled to it at the end.
+// TMEM (512 columns): O_r [0, 256), S buffers [256, 352), Q dims 0..319 as
+// BF16 pairs [352, 512). Shared memory: Q dims 320..511 and the 64 rope dims
+// (128-byte swizzle), the gathered rows (4 stages x 32 rows x 1152 B) and P.
+//
+// Warp roles (12 warps): 0-3 gather (warp w owns stage w: 16-byte cp.async of
+// the indexed rows into swizzled K-major tiles plus a validity bitmask);
+// 4-6 issue the QK MMAs; 7 issues the PV MMAs; 8-11 run the softmax, one head
+// row per thread, load Q per item and write the output. The online softmax
+// keeps the reference's semantics (dsa/workspace.py:242-318): invalid index
+// -> -inf, FP32 max/sum, BF16 P, FP32 O. O is only rescaled when the row max
+// grows by more than 2^8 in exp2 units (lazy rescale); the reported max is
+// the true max and the sum is rescaled to it at the end.
 //
 // No TMA and no clusters are used. Every wait is bounded and reports through
 // the status word.
@@ -40,17 +45,21 @@ using namespace umma;
 constexpr int kUmBN = 32;          // keys per tile
 constexpr int kUmStages = 4;       // gather pipeline depth (one gather warp per stage)
 constexpr int kGatherWarps = kUmStages;
-constexpr int kMmaWarp = kGatherWarps;          // 4
-constexpr int kSoftWarp0 = kMmaWarp + 1;        // 5
+constexpr int kQkIssuers = 3;      // QK issuer warps, one S buffer each
+constexpr int kQkWarp0 = kGatherWarps;                  // 4
+constexpr int kPvWarp = kQkWarp0 + kQkIssuers;          // 7
+constexpr int kSoftWarp0 = kPvWarp + 1;                 // 8
 constexpr int kSoftWarps = 4;
-constexpr int kUmThreads = 32 * (kSoftWarp0 + kSoftWarps);  // 288
+constexpr int kUmThreads = 32 * (kSoftWarp0 + kSoftWarps);  // 384
 constexpr int kUmHeads = 128;
-constexpr int kQTmemDims = 384;    // Q latent dims kept in TMEM
+constexpr int kQTmemDims = 320;    // Q dims kept in TMEM (A operand of TS steps)
+constexpr int kQkSteps = kDimQK / 16;        // 36
+constexpr int kTsSteps = kQTmemDims / 16;    // 20
 
 // Shared-memory layout (bytes from a 1024-aligned base).
 constexpr uint32_t kQBlock = 128u * 128u;                    // 128 heads x 64 dims (SW128)
-constexpr uint32_t kOffQ = 0;                                // Q dims 384..511 (2 blocks) + rope (1 block)
-constexpr uint32_t kQBytes = 3u * kQBlock;                   // 49152
+constexpr uint32_t kOffQ = 0;                                // Q dims 320..511 (3 blocks) + rope (1 block)
+constexpr uint32_t kQBytes = 4u * kQBlock;                   // 65536
 constexpr uint32_t kKBlock = (uint32_t)kUmBN * 128u;         // 4096: 32 keys x 64 dims (SW128)
 constexpr uint32_t kKStage = 9u * kKBlock;                   // 8 latent blocks + 1 rope block
 constexpr uint32_t kOffK = kOffQ + kQBytes;
@@ -62,10 +71,11 @@ constexpr uint32_t kOffBar = kOffMask + 64u;
 enum Bar {
   kFull0 = 0,
   kEmpty0 = kFull0 + kUmStages,
-  kQFull = kEmpty0 + kUmStages,
+  kQFull = kEmpty0 + kUmStages,  // this item's Q is loaded (softmax warps)
+  kQSeen,                        // every QK issuer has seen this item's Q (issuers)
   kSFull0,
-  kSFree0 = kSFull0 + 2,
-  kPFull = kSFree0 + 2,
+  kSFree0 = kSFull0 + kQkIssuers,
+  kPFull = kSFree0 + kQkIssuers,
   kPvDone,
   kBarCount
 };
@@ -77,10 +87,11 @@ constexpr uint32_t kSmemBytes = kSmemUsed + 1024u;  // slack for the 1024-byte a
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 0;
 constexpr uint32_t kTmemS = 256;
-constexpr uint32_t kTmemQ = 320;
+constexpr uint32_t kTmemQ = kTmemS + kQkIssuers * kUmBN;    // 352
 
 static_assert(kOffK % 1024 == 0 && kKStage % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms");
 static_assert(kTmemQ + kQTmemDims / 2 == kTmemCols, "TMEM budget");
+static_assert(kQTmemDims % 64 == 0, "Q TMEM part is a whole number of 64-dim blocks");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct Item {
@@ -132,7 +143,8 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       mbar_init(bar(kEmpty0 + s), 1);
     }
     mbar_init(bar(kQFull), kSoftWarps);
-    for (int k = 0; k < 2; ++k) {
+    mbar_init(bar(kQSeen), kQkIssuers);
+    for (int k = 0; k < kQkIssuers; ++k) {
       mbar_init(bar(kSFull0 + k), 1);
       mbar_init(bar(kSFree0 + k), kSoftWarps);
     }
@@ -200,60 +212,73 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       }
     }
     if (!ok) report_error(p.status, kErrTimeout);
-  } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer (one lane) ----------------
+  } else if (warp < kPvWarp) {
+    // ---------------- QK issuer i: tiles g with g % 3 == i, into S buffer i ----------------
     if (lane == 0) {
+      const uint32_t i = (uint32_t)(warp - kQkWarp0);
       const uint32_t idesc_qk = idesc_bf16(128, kUmBN, false, false);
-      const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
-      uint32_t g = 0, it = 0;
+      const uint32_t d = tmem + kTmemS + i * kUmBN;
+      uint32_t g = 0, it = 0, n = 0;  // n: tiles this issuer ran
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
         const Item w = make_item(p, item);
-        const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
-        auto issue_pv = [&](uint32_t gp, bool first) -> bool {
-          if (!mbar_wait(bar(kPFull), gp & 1u, abort_flag)) return false;
-          tc_fence_after();
-          const uint32_t stage = base + kOffK + (gp % kUmStages) * kKStage;
-#pragma unroll
-          for (int j = 0; j < kUmBN / 16; ++j) {
-            const uint64_t ad = smem_desc(base + kOffP + j * 32, 16, 512, kLayoutSw64);
-            const uint64_t bd = smem_desc(stage + vblk + j * 2048, kKBlock, 1024, kLayoutSw128);
-            mma_bf16_ss(tmem + kTmemO, ad, bd, idesc_pv, (first && j == 0) ? 0u : 1u);
-          }
-          mma_commit(bar(kPvDone));
-          mma_commit(bar(kEmpty0 + gp % kUmStages));
-          return true;
-        };
+        // Every issuer observes every item's Q (even without a tile in it) and
+        // acknowledges, so no issuer can fall a barrier phase behind.
         ok = mbar_wait(bar(kQFull), it & 1u, abort_flag);
-        tc_fence_after();
+        if (!ok) break;
+        mbar_arrive(bar(kQSeen));
         for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
+          if (g % kQkIssuers != i) continue;
           const uint32_t s = g % kUmStages;
-          const uint32_t b = g & 1u;
           ok = mbar_wait(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
-          if (ok && g >= 2) ok = mbar_wait(bar(kSFree0 + b), ((g - 2) >> 1) & 1u, abort_flag);
+          if (ok && n > 0) ok = mbar_wait(bar(kSFree0 + i), (n - 1) & 1u, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t stage = base + kOffK + s * kKStage;
-          const uint32_t d = tmem + kTmemS + b * kUmBN;
 #pragma unroll
-          for (int ks = 0; ks < kQTmemDims / 16; ++ks) {  // dims 0..383: A = Q from TMEM
+          for (int ks = 0; ks < kTsSteps; ++ks) {  // dims 0..319: A = Q from TMEM
             const uint64_t bd =
                 smem_desc(stage + (ks >> 2) * kKBlock + (uint32_t)(ks & 3) * 32u, 16, 1024, kLayoutSw128);
             mma_bf16_ts(d, tmem + kTmemQ + (uint32_t)ks * 8u, bd, idesc_qk, ks > 0 ? 1u : 0u);
           }
 #pragma unroll
-          for (int ks = kQTmemDims / 16; ks < kDimQK / 16; ++ks) {  // dims 384..575: A from smem
-            const uint32_t qb = (uint32_t)(ks - kQTmemDims / 16) >> 2;
+          for (int ks = kTsSteps; ks < kQkSteps; ++ks) {  // dims 320..575: A from shared memory
+            const uint32_t qb = (uint32_t)(ks - kTsSteps) >> 2;
             const uint64_t ad = smem_desc(base + kOffQ + qb * kQBlock + (uint32_t)(ks & 3) * 32u, 16, 1024,
                                           kLayoutSw128);
             const uint64_t bd =
                 smem_desc(stage + (ks >> 2) * kKBlock + (uint32_t)(ks & 3) * 32u, 16, 1024, kLayoutSw128);
             mma_bf16_ss(d, ad, bd, idesc_qk, 1u);
           }
-          mma_commit(bar(kSFull0 + b));
-          if (t > 0) ok = issue_pv(g - 1, t == 1);
+          mma_commit(bar(kSFull0 + i));
+          ++n;
         }
-        if (ok) ok = issue_pv(g - 1, w.ntiles == 1);
+      }
+      if (!ok) report_error(p.status, kErrTimeout);
+    }
+  } else if (warp == kPvWarp) {
+    // ---------------- PV issuer: every tile in order ----------------
+    if (lane == 0) {
+      const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
+      uint32_t g = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const Item w = make_item(p, item);
+        const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
+        for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
+          ok = mbar_wait(bar(kPFull), g & 1u, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t stage = base + kOffK + (g % kUmStages) * kKStage;
+#pragma unroll
+          for (int j = 0; j < kUmBN / 16; ++j) {
+            const uint64_t ad = smem_desc(base + kOffP + j * 32, 16, 512, kLayoutSw64);
+            const uint64_t bd = smem_desc(stage + vblk + j * 2048, kKBlock, 1024, kLayoutSw128);
+            mma_bf16_ss(tmem + kTmemO, ad, bd, idesc_pv, (t == 0 && j == 0) ? 0u : 1u);
+          }
+          mma_commit(bar(kPvDone));
+          mma_commit(bar(kEmpty0 + g % kUmStages));
+        }
       }
       if (!ok) report_error(p.status, kErrTimeout);
     }
@@ -269,9 +294,11 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
-      // Q of this head row: dims 0..383 -> TMEM, dims 384..511 and the rope
-      // dims -> shared memory (128-byte swizzle). The previous item's MMAs are
-      // complete (its epilogue waited for its last PV).
+      // Q of this head row: dims 0..319 -> TMEM, dims 320..511 and the rope
+      // dims -> shared memory (128-byte swizzle). The previous item's MMAs
+      // are complete (its epilogue waited for its last PV), and every QK
+      // issuer has seen the previous item's Q.
+      if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag))) break;
       {
         const size_t qrow = (size_t)w.token * kUmHeads + row;
         const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
@@ -279,24 +306,24 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         for (int ch = 0; ch < kQTmemDims / 64; ++ch) {
           uint32_t r[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint4 v = __ldg(src + ch * 8 + i);
-            r[4 * i] = v.x;
-            r[4 * i + 1] = v.y;
-            r[4 * i + 2] = v.z;
-            r[4 * i + 3] = v.w;
+          for (int k = 0; k < 8; ++k) {
+            const uint4 v = __ldg(src + ch * 8 + k);
+            r[4 * k] = v.x;
+            r[4 * k + 1] = v.y;
+            r[4 * k + 2] = v.z;
+            r[4 * k + 3] = v.w;
           }
           tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
         }
         uint8_t* const qdst = sbase + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)  // latent dims 384..511: 2 blocks x 8 chunks
-          *reinterpret_cast<uint4*>(qdst + (i >> 3) * kQBlock + (((i & 7) ^ (row & 7)) * 16)) =
-              __ldg(src + kQTmemDims / 8 + i);
+        for (int k = 0; k < (kDimLatent - kQTmemDims) / 8; ++k)  // latent dims 320..511: 3 blocks
+          *reinterpret_cast<uint4*>(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16)) =
+              __ldg(src + kQTmemDims / 8 + k);
         const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          *reinterpret_cast<uint4*>(qdst + 2 * kQBlock + ((i ^ (row & 7)) * 16)) = __ldg(rsrc + i);
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint4*>(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16)) = __ldg(rsrc + k);
         fence_proxy_async_smem();
         tmem_wait_st();
         tc_fence_before();
@@ -306,21 +333,22 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       float m_true = kNegFltMax, m_used = kNegFltMax, l = 0.f;
       for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
         const uint32_t s = g % kUmStages;
-        const uint32_t b = g & 1u;
-        ok = wait_warp(bar(kSFull0 + b), (g >> 1) & 1u, abort_flag);
+        const uint32_t i = g % kQkIssuers;
+        const uint32_t n = g / kQkIssuers;  // uses of S buffer i so far
+        ok = wait_warp(bar(kSFull0 + i), n & 1u, abort_flag);
         if (!ok) break;
         tc_fence_after();
         float x[32];
         {
           uint32_t sv[32];
-          tmem_ld32(tmem + t_lane + kTmemS + b * kUmBN, sv);
+          tmem_ld32(tmem + t_lane + kTmemS + i * kUmBN, sv);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = u2f(sv[i]);
+          for (int k = 0; k < 32; ++k) x[k] = u2f(sv[k]);
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kSFree0 + b));
+        if (lane == 0) mbar_arrive(bar(kSFree0 + i));
         // validity bits of the tile's keys (written by the gather warp)
         ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
         if (!ok) break;
@@ -367,7 +395,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
             tmem_ld32(a, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
+            for (int k = 0; k < 32; ++k) o[k] = f2u(u2f(o[k]) * alpha);
             tmem_st32(a, o);
           }
           tmem_wait_st();
@@ -393,11 +421,11 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
           tmem_wait_ld();
           uint32_t h[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            h[i] = pack_bf16x2(__fdiv_rn(u2f(o[2 * i]), l), __fdiv_rn(u2f(o[2 * i + 1]), l));
+          for (int k = 0; k < 16; ++k)
+            h[k] = pack_bf16x2(__fdiv_rn(u2f(o[2 * k]), l), __fdiv_rn(u2f(o[2 * k + 1]), l));
           uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+          for (int k = 0; k < 4; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
         }
         if (w.half == 0) {
           p.out_max[orow] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, 24.0f);
@@ -413,9 +441,9 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
           tmem_wait_ld();
           float4* d4 = reinterpret_cast<float4*>(dst + cb);
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(u2f(o[4 * i]) * f, u2f(o[4 * i + 1]) * f, u2f(o[4 * i + 2]) * f,
-                                u2f(o[4 * i + 3]) * f);
+          for (int k = 0; k < 8; ++k)
+            d4[k] = make_float4(u2f(o[4 * k]) * f, u2f(o[4 * k + 1]) * f, u2f(o[4 * k + 2]) * f,
+                                u2f(o[4 * k + 3]) * f);
         }
         if (w.half == 0) {
           p.part_max[prow_idx] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, 24.0f);
