@@ -63,9 +63,9 @@ constexpr uint32_t kQBytes = 4u * kQBlock;                   // 65536
 constexpr uint32_t kKBlock = (uint32_t)kUmBN * 128u;         // 4096: 32 keys x 64 dims (SW128)
 constexpr uint32_t kKStage = 9u * kKBlock;                   // 8 latent blocks + 1 rope block
 constexpr uint32_t kOffK = kOffQ + kQBytes;
-constexpr uint32_t kOffP = kOffK + kUmStages * kKStage;      // P: 128 rows x 32 keys (SW64)
-constexpr uint32_t kPBytes = 128u * (uint32_t)kUmBN * 2u;    // 8192
-constexpr uint32_t kOffMask = kOffP + kPBytes;               // validity bits per stage
+constexpr uint32_t kOffP = kOffK + kUmStages * kKStage;      // P: 2 x (128 rows x 32 keys, SW64)
+constexpr uint32_t kPBytes = 128u * (uint32_t)kUmBN * 2u;    // 8192 per buffer
+constexpr uint32_t kOffMask = kOffP + 2u * kPBytes;          // validity bits per stage
 constexpr uint32_t kOffBar = kOffMask + 64u;
 
 enum Bar {
@@ -75,9 +75,9 @@ enum Bar {
   kQSeen,                        // every QK issuer has seen this item's Q (issuers)
   kSFull0,
   kSFree0 = kSFull0 + kQkIssuers,
-  kPFull = kSFree0 + kQkIssuers,
-  kPvDone,
-  kBarCount
+  kPFull0 = kSFree0 + kQkIssuers,  // P buffer b written (tiles g with g % 2 == b)
+  kPvDone0 = kPFull0 + 2,          // PV of tiles g with g % 2 == b done (P buffer b free)
+  kBarCount = kPvDone0 + 2
 };
 constexpr uint32_t kOffTmemSlot = kOffBar + kBarCount * 8u;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 8u;
@@ -108,6 +108,38 @@ __device__ __forceinline__ Item make_item(const FwdParams& p, int item) {
   split_bounds(p.topk, kUmBN, p.split, it.sp, &it.kbeg, &it.kend);
   it.ntiles = (it.kend - it.kbeg + kUmBN - 1) / kUmBN;
   return it;
+}
+
+// Position of one tile in this CTA's sequence of tiles (items blockIdx.x,
+// blockIdx.x + gridDim.x, ...; tiles 0..ntiles-1 of each).
+struct TileCursor {
+  int item, t;
+  Item w;
+};
+
+__device__ __forceinline__ void cursor_advance(const FwdParams& p, int n_items, TileCursor& c, int k) {
+  c.t += k;
+  while (c.item < n_items && c.t >= c.w.ntiles) {
+    c.t -= c.w.ntiles;
+    c.item += gridDim.x;
+    if (c.item < n_items) c.w = make_item(p, c.item);
+  }
+}
+
+__device__ __forceinline__ TileCursor cursor_start(const FwdParams& p, int n_items, int k) {
+  TileCursor c;
+  c.item = blockIdx.x;
+  c.t = 0;
+  if (c.item < n_items) c.w = make_item(p, c.item);
+  cursor_advance(p, n_items, c, k);
+  return c;
+}
+
+// Index of key `lane` of the cursor's tile (-1 past the split's end or past the last item).
+__device__ __forceinline__ int cursor_index(const FwdParams& p, const TileCursor& c, int lane) {
+  if (c.item >= p.tokens * p.split * 2) return -1;
+  const int j = c.w.kbeg + c.t * kUmBN + lane;
+  return j < c.w.kend ? __ldg(p.ids + (size_t)c.w.token * p.topk + j) : -1;
 }
 
 __device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(v); }
@@ -148,8 +180,10 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       mbar_init(bar(kSFull0 + k), 1);
       mbar_init(bar(kSFree0 + k), kSoftWarps);
     }
-    mbar_init(bar(kPFull), kSoftWarps);
-    mbar_init(bar(kPvDone), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(kPFull0 + b), kSoftWarps);
+      mbar_init(bar(kPvDone0 + b), 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -167,74 +201,84 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
 
   if (warp < kGatherWarps) {
     // ---------------- gather: warp w fills stage w for tiles g = w, w+4, ... ----------------
+    // The indices of the tile two rounds ahead are loaded one round early, so
+    // a freed stage waits only for its rows.
     const uint32_t s = (uint32_t)warp;
     const uint32_t stage = base + kOffK + s * kKStage;
     uint32_t* const mask_s = reinterpret_cast<uint32_t*>(sbase + kOffMask) + s;
-    uint32_t g = 0, n = 0;  // g: tile counter of this CTA, n: tiles this warp filled
-    bool ok = true;
     // lane -> (key quarter kq, 16-byte chunk j8): 4 rows x 128 contiguous bytes per instruction
     const int j8 = lane & 7;
     const int kq = lane >> 3;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const Item w = make_item(p, item);
-      const int32_t* ids_t = p.ids + (size_t)w.token * p.topk;
-      const __nv_bfloat16* const kv_b = p.kv + (size_t)w.batch * L * kDimLatent;
-      const __nv_bfloat16* const kr_b = p.k_rope + (size_t)w.batch * L * kDimRope;
-      for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
-        if (g % kUmStages != s) continue;
-        if (n > 0) {  // the stage's previous tile (g - 4) has been consumed by its PV
-          if (lane == 0) ok = mbar_wait(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag);
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          if (!ok) break;
-        }
-        const int j = w.kbeg + t * kUmBN + lane;
-        const int idx = j < w.kend ? __ldg(ids_t + j) : -1;
-        const int row = min(max(idx, 0), L - 1);  // clamped address; masked below
-        const uint32_t bits = __ballot_sync(0xffffffffu, (idx >= 0) & (idx < L));
-        if (lane == 0) *mask_s = bits;
-#pragma unroll 2
-        for (int i = 0; i < kUmBN / 4; ++i) {
-          const int k = kq + 4 * i;
-          const int rk = __shfl_sync(0xffffffffu, row, k);
-          const uint32_t dst = stage + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u +
-                               (uint32_t)((j8 ^ (k & 7)) * 16);
-          const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
-#pragma unroll
-          for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * kKBlock, src + kb * 64);
-          cp_async_16(dst + 8 * kKBlock, kr_b + (size_t)rk * kDimRope + j8 * 8);
-        }
-        cp_async_commit();
-        cp_async_wait<0>();
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kFull0 + s));
-        ++n;
+    TileCursor cur = cursor_start(p, n_items, (int)s);
+    TileCursor nx = cur;
+    cursor_advance(p, n_items, nx, kUmStages);
+    TileCursor nx2 = nx;
+    cursor_advance(p, n_items, nx2, kUmStages);
+    int idx_cur = cursor_index(p, cur, lane);
+    int idx_nx = cursor_index(p, nx, lane);
+    uint32_t n = 0;  // tiles this warp filled
+    bool ok = true;
+    while (cur.item < n_items) {
+      if (n > 0) {  // the stage's previous tile has been consumed by its PV
+        if (lane == 0) ok = mbar_wait(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
       }
+      const int row = min(max(idx_cur, 0), L - 1);  // clamped address; masked below
+      const uint32_t bits = __ballot_sync(0xffffffffu, (idx_cur >= 0) & (idx_cur < L));
+      if (lane == 0) *mask_s = bits;
+      const __nv_bfloat16* const kv_b = p.kv + (size_t)cur.w.batch * L * kDimLatent;
+      const __nv_bfloat16* const kr_b = p.k_rope + (size_t)cur.w.batch * L * kDimRope;
+#pragma unroll 2
+      for (int i = 0; i < kUmBN / 4; ++i) {
+        const int k = kq + 4 * i;
+        const int rk = __shfl_sync(0xffffffffu, row, k);
+        const uint32_t dst = stage + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u +
+                             (uint32_t)((j8 ^ (k & 7)) * 16);
+        const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * kKBlock, src + kb * 64);
+        cp_async_16(dst + 8 * kKBlock, kr_b + (size_t)rk * kDimRope + j8 * 8);
+      }
+      cp_async_commit();
+      const int idx_nx2 = cursor_index(p, nx2, lane);  // consumed one round later
+      cp_async_wait<0>();
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kFull0 + s));
+      ++n;
+      cur = nx;
+      nx = nx2;
+      cursor_advance(p, n_items, nx2, kUmStages);
+      idx_cur = idx_nx;
+      idx_nx = idx_nx2;
     }
     if (!ok) report_error(p.status, kErrTimeout);
   } else if (warp < kPvWarp) {
     // ---------------- QK issuer i: tiles g with g % 3 == i, into S buffer i ----------------
-    if (lane == 0) {
-      const uint32_t i = (uint32_t)(warp - kQkWarp0);
-      const uint32_t idesc_qk = idesc_bf16(128, kUmBN, false, false);
-      const uint32_t d = tmem + kTmemS + i * kUmBN;
-      uint32_t g = 0, it = 0, n = 0;  // n: tiles this issuer ran
-      bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-        const Item w = make_item(p, item);
-        // Every issuer observes every item's Q (even without a tile in it) and
-        // acknowledges, so no issuer can fall a barrier phase behind.
-        ok = mbar_wait(bar(kQFull), it & 1u, abort_flag);
+    // The whole warp runs the loop and waits; one elected lane issues.
+    const uint32_t i = (uint32_t)(warp - kQkWarp0);
+    const uint32_t idesc_qk = idesc_bf16(128, kUmBN, false, false);
+    const uint32_t d = tmem + kTmemS + i * kUmBN;
+    uint32_t g = 0, it = 0, n = 0;  // n: tiles this issuer ran
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+      const Item w = make_item(p, item);
+      // Every issuer observes every item's Q (even without a tile in it) and
+      // acknowledges, so no issuer can fall a barrier phase behind.
+      ok = wait_warp(bar(kQFull), it & 1u, abort_flag);
+      if (!ok) break;
+      if (elect_one()) mbar_arrive(bar(kQSeen));
+      __syncwarp();
+      for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
+        if (g % kQkIssuers != i) continue;
+        const uint32_t s = g % kUmStages;
+        ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
+        if (ok && n > 0) ok = wait_warp(bar(kSFree0 + i), (n - 1) & 1u, abort_flag);
         if (!ok) break;
-        mbar_arrive(bar(kQSeen));
-        for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
-          if (g % kQkIssuers != i) continue;
-          const uint32_t s = g % kUmStages;
-          ok = mbar_wait(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
-          if (ok && n > 0) ok = mbar_wait(bar(kSFree0 + i), (n - 1) & 1u, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t stage = base + kOffK + s * kKStage;
+        tc_fence_after();
+        const uint32_t stage = base + kOffK + s * kKStage;
+        if (elect_one()) {
 #pragma unroll
           for (int ks = 0; ks < kTsSteps; ++ks) {  // dims 0..319: A = Q from TMEM
             const uint64_t bd =
@@ -251,44 +295,46 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
             mma_bf16_ss(d, ad, bd, idesc_qk, 1u);
           }
           mma_commit(bar(kSFull0 + i));
-          ++n;
         }
+        __syncwarp();
+        ++n;
       }
-      if (!ok) report_error(p.status, kErrTimeout);
     }
+    if (!ok && lane == 0) report_error(p.status, kErrTimeout);
   } else if (warp == kPvWarp) {
-    // ---------------- PV issuer: every tile in order ----------------
-    if (lane == 0) {
-      const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
-      uint32_t g = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const Item w = make_item(p, item);
-        const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
-        for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
-          ok = mbar_wait(bar(kPFull), g & 1u, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t stage = base + kOffK + (g % kUmStages) * kKStage;
+    // ---------------- PV issuer: every tile in order (warp-converged, one elected lane issues) ----
+    const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const Item w = make_item(p, item);
+      const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
+      for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
+        ok = wait_warp(bar(kPFull0 + (g & 1u)), (g >> 1) & 1u, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t stage = base + kOffK + (g % kUmStages) * kKStage;
+        if (elect_one()) {
 #pragma unroll
           for (int j = 0; j < kUmBN / 16; ++j) {
-            const uint64_t ad = smem_desc(base + kOffP + j * 32, 16, 512, kLayoutSw64);
+            const uint64_t ad = smem_desc(base + kOffP + (g & 1u) * kPBytes + j * 32, 16, 512, kLayoutSw64);
             const uint64_t bd = smem_desc(stage + vblk + j * 2048, kKBlock, 1024, kLayoutSw128);
             mma_bf16_ss(tmem + kTmemO, ad, bd, idesc_pv, (t == 0 && j == 0) ? 0u : 1u);
           }
-          mma_commit(bar(kPvDone));
+          mma_commit(bar(kPvDone0 + (g & 1u)));
           mma_commit(bar(kEmpty0 + g % kUmStages));
         }
+        __syncwarp();
       }
-      if (!ok) report_error(p.status, kErrTimeout);
     }
+    if (!ok && lane == 0) report_error(p.status, kErrTimeout);
   } else {
     // ---------------- softmax + epilogue (one head row per thread) ----------------
     const int quad = warp & 3;  // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;
     const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
     const float c = 1.4426950408889634f / 24.0f;  // log2(e) / 24
-    uint8_t* const prow = sbase + kOffP + (uint32_t)(row >> 3) * 512u + (uint32_t)(row & 7) * 64u;
+    uint8_t* const prow0 = sbase + kOffP + (uint32_t)(row >> 3) * 512u + (uint32_t)(row & 7) * 64u;
     const uint32_t* const mask_all = reinterpret_cast<const uint32_t*>(sbase + kOffMask);
     uint32_t g = 0, it = 0;
     bool ok = true;
@@ -378,15 +424,20 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
           packed[k / 2] = pack_bf16x2(p0, p1);
         }
         l = l * alpha + sum;
-        // P (single buffer) is free once the previous PV finished reading it
-        if (g >= 1) ok = wait_warp(bar(kPvDone), (g - 1) & 1u, abort_flag);
+        // P buffer g % 2 is free once PV(g - 2) finished reading it
+        const uint32_t pb = g & 1u;
+        if (g >= 2) ok = wait_warp(bar(kPvDone0 + pb), ((g >> 1) - 1) & 1u, abort_flag);
         if (!ok) break;
+        uint8_t* const prow = prow0 + pb * kPBytes;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           *reinterpret_cast<uint4*>(prow + ((q ^ ((row & 7) >> 1)) * 16)) =
               make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
         fence_proxy_async_smem();
         if (__any_sync(0xffffffffu, resc) && t > 0) {
+          // O is read and rescaled: PV(g - 1) must have finished writing it
+          ok = wait_warp(bar(kPvDone0 + (pb ^ 1u)), ((g - 1) >> 1) & 1u, abort_flag);
+          if (!ok) break;
           tc_fence_after();
           uint32_t o[32];
 #pragma unroll 1
@@ -402,11 +453,11 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kPFull));
+        if (lane == 0) mbar_arrive(bar(kPFull0 + pb));
       }
       if (!ok) break;
       // ---- epilogue: this CTA's 256 dims of the head row -> output (or FP32 partial) ----
-      ok = wait_warp(bar(kPvDone), (g - 1) & 1u, abort_flag);
+      ok = wait_warp(bar(kPvDone0 + ((g - 1) & 1u)), ((g - 1) >> 1) & 1u, abort_flag);
       if (!ok) break;
       tc_fence_after();
       const float f = (m_true == kNegFltMax) ? 1.f : ex2((m_used - m_true) * c);
