@@ -24,6 +24,7 @@ STATUS_CUDA_ERROR = 6
 FAMILY_AUTO = 0
 FAMILY_WARP_MMA = 1
 FAMILY_UMMA = 2
+FAMILY_UMMA_PAIR = 3
 
 # Every entry point declared in include/dsa_b200.h.
 EXPORTS = (

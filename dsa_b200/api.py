@@ -23,7 +23,8 @@ DEVICE_TYPE = "cuda"
 
 LaunchRecord = namedtuple("LaunchRecord", "name family heads_per_cta keys_per_tile split")
 
-_FAMILY_NAMES = {_native.FAMILY_WARP_MMA: "warp_mma", _native.FAMILY_UMMA: "umma"}
+_FAMILY_NAMES = {_native.FAMILY_WARP_MMA: "warp_mma", _native.FAMILY_UMMA: "umma",
+                 _native.FAMILY_UMMA_PAIR: "umma_pair"}
 
 
 def _check_inputs(q, kv, q_rope, k_rope, indices):
@@ -74,7 +75,8 @@ def _check_tuning(config, shape, cores):
 
 def _launch_from_tuning(config, shape):
     if config.bm == 128:
-        launch = _native.Launch(_native.FAMILY_UMMA, 128, config.bn, config.split)
+        family = _native.FAMILY_UMMA_PAIR if config.pv_cols == 512 else _native.FAMILY_UMMA
+        launch = _native.Launch(family, 128, config.bn, config.split)
     else:
         launch = _native.Launch(_native.FAMILY_WARP_MMA, 16, config.bn, config.split)
     code = _native.load().dsa_check_launch(*shape, ctypes.byref(launch))

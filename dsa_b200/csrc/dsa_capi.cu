@@ -84,7 +84,8 @@ int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t leng
       if (bn != 32 && bn != 64) return DSA_STATUS_UNSUPPORTED;
       break;
     }
-    case DSA_FAMILY_UMMA: {
+    case DSA_FAMILY_UMMA:
+    case DSA_FAMILY_UMMA_PAIR: {
       if (launch->heads_per_cta != 128 || heads != 128 || bn != 32) return DSA_STATUS_UNSUPPORTED;
       break;
     }
@@ -103,11 +104,21 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
   if (heads % 16 != 0) return DSA_STATUS_UNSUPPORTED;
   dsa_launch_t e;
   if (heads == 128) {
-    // tcgen05 family: persistent CTAs over (token, split, V half) items;
-    // split the TOPK range only until every resident CTA has an item.
-    e.family = DSA_FAMILY_UMMA;
     e.heads_per_cta = 128;
     e.keys_per_tile = 32;
+    const int pair_ctas = dsa::pair_max_ctas();
+    if (pair_ctas > 0 && batch * queries >= pair_ctas / 2) {
+      // pair family: one (score CTA, value CTA) cluster per query; enough
+      // queries to occupy every cluster without splitting the TOPK range.
+      e.family = DSA_FAMILY_UMMA_PAIR;
+      e.split = 1;
+      *out = e;
+      return DSA_STATUS_OK;
+    }
+    // split-V family for few queries: persistent CTAs over (token, split,
+    // V half) items; split the TOPK range only until every resident CTA has
+    // an item.
+    e.family = DSA_FAMILY_UMMA;
     int ctas = dsa::umma_max_ctas();
     if (ctas <= 0) ctas = sm_count();
     const int64_t halves = 2 * batch * queries;
@@ -207,6 +218,7 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
   switch (e.family) {
     case DSA_FAMILY_WARP_MMA: err = dsa::launch_fwd_warp_mma(p, s); break;
     case DSA_FAMILY_UMMA: err = dsa::launch_fwd_umma(p, s); break;
+    case DSA_FAMILY_UMMA_PAIR: err = dsa::launch_fwd_pair(p, s); break;
     default: return DSA_STATUS_UNSUPPORTED;
   }
   if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;

@@ -118,6 +118,9 @@ cudaError_t launch_fwd_warp_mma(const FwdParams& p, cudaStream_t stream);
 cudaError_t launch_fwd_umma(const FwdParams& p, cudaStream_t stream);
 // CTAs of the umma family that fit on the current device at once (-1 on error).
 int umma_max_ctas();
+cudaError_t launch_fwd_pair(const FwdParams& p, cudaStream_t stream);
+// CTAs of the pair family (two per cluster) resident at once (-1 on error).
+int pair_max_ctas();
 cudaError_t launch_merge(const float* num, const float* pmax, const float* psum,
                          __nv_bfloat16* out, float* omax, float* osum, int tokens, int heads,
                          int split, cudaStream_t stream);

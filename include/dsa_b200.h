@@ -65,7 +65,10 @@ typedef enum dsa_status {
 typedef enum dsa_family {
   DSA_FAMILY_AUTO = 0,      /* pick by shape (dsa_default_launch) */
   DSA_FAMILY_WARP_MMA = 1,  /* generic: 16 heads per CTA, warp-level MMA, any H % 16 == 0 */
-  DSA_FAMILY_UMMA = 2       /* tcgen05/TMEM path: 2-CTA cluster, 128 heads per query */
+  DSA_FAMILY_UMMA = 2,      /* tcgen05/TMEM path, H == 128: one CTA per (query, half of the 512
+                               value columns); each CTA computes the full scores */
+  DSA_FAMILY_UMMA_PAIR = 3  /* tcgen05/TMEM path, H == 128: a 2-CTA cluster per query, one CTA
+                               computes scores + softmax, the other P.V over all 512 columns */
 } dsa_family_t;
 
 /* One entry of the shape-keyed launch table (reference: Tuning,
