@@ -3,7 +3,7 @@
 Drop-in for ``dsa.forward`` (dsa/__init__.py:2-5 of the reference):
 ``import dsa_b200 as dsa; dsa.forward(q, kv, q_rope, k_rope, indices)``.
 """
-from .api import device_status, forward
+from .api import ForwardPlan, device_status, forward
 from .config import CASE_SHAPES, SELECTED, Tuning
 
-__all__ = ["forward", "Tuning", "CASE_SHAPES", "SELECTED", "device_status"]
+__all__ = ["forward", "ForwardPlan", "Tuning", "CASE_SHAPES", "SELECTED", "device_status"]

@@ -25,6 +25,7 @@ FAMILY_AUTO = 0
 FAMILY_WARP_MMA = 1
 FAMILY_UMMA = 2
 FAMILY_UMMA_PAIR = 3
+FAMILY_STREAM = 4
 
 # Every entry point declared in include/dsa_b200.h.
 EXPORTS = (

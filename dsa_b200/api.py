@@ -24,7 +24,7 @@ DEVICE_TYPE = "cuda"
 LaunchRecord = namedtuple("LaunchRecord", "name family heads_per_cta keys_per_tile split")
 
 _FAMILY_NAMES = {_native.FAMILY_WARP_MMA: "warp_mma", _native.FAMILY_UMMA: "umma",
-                 _native.FAMILY_UMMA_PAIR: "umma_pair"}
+                 _native.FAMILY_UMMA_PAIR: "umma_pair", _native.FAMILY_STREAM: "stream"}
 
 
 def _check_inputs(q, kv, q_rope, k_rope, indices):
@@ -77,6 +77,8 @@ def _launch_from_tuning(config, shape):
     if config.bm == 128:
         family = _native.FAMILY_UMMA_PAIR if config.pv_cols == 512 else _native.FAMILY_UMMA
         launch = _native.Launch(family, 128, config.bn, config.split)
+    elif config.bn == 32:
+        launch = _native.Launch(_native.FAMILY_STREAM, 16, config.bn, config.split)
     else:
         launch = _native.Launch(_native.FAMILY_WARP_MMA, 16, config.bn, config.split)
     code = _native.load().dsa_check_launch(*shape, ctypes.byref(launch))
@@ -186,3 +188,57 @@ def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_ker
                                         launch.keys_per_tile, launch.split))
         return result, tuple(records)
     return result
+
+
+class ForwardPlan:
+    """``forward`` prepared once for fixed input tensors.
+
+    Checks the inputs, picks the launch entry and allocates the outputs and
+    the split-KV workspace at construction; ``run()`` then only enqueues the
+    kernels on the current stream (no allocation, no host synchronisation),
+    so a serving loop can call it per step or capture it in a CUDA graph.
+    The plan keeps references to its inputs: callers update them in place
+    (same addresses) between runs. Results are written into the same
+    ``(output, softmax_max, softmax_sum)`` tensors every run.
+    """
+
+    def __init__(self, q, kv, q_rope, k_rope, indices, *, config=None, cores=28):
+        shape, device = _check_inputs(q, kv, q_rope, k_rope, indices)
+        if config is None:
+            _check_cores(cores)
+            launch = _default_launch(shape, device)
+        else:
+            _check_tuning(config, shape, cores)
+            launch = _launch_from_tuning(config, shape)
+        batch, queries, heads, _, _ = shape
+        self.inputs = (q, kv, q_rope, k_rope, indices)
+        self.device = device
+        self.launch = launch
+        self.outputs = (torch.empty_like(q),
+                        torch.empty((batch, 1, queries, heads), device=device, dtype=torch.float32),
+                        torch.empty((batch, 1, queries, heads), device=device, dtype=torch.float32))
+        args = _native.FwdArgs()
+        args.q, args.kv, args.q_rope, args.k_rope = q.data_ptr(), kv.data_ptr(), q_rope.data_ptr(), k_rope.data_ptr()
+        args.indices = indices.data_ptr()
+        args.output, args.softmax_max, args.softmax_sum = (t.data_ptr() for t in self.outputs)
+        args.batch, args.queries, args.heads, args.length, args.topk = shape
+        args.launch = launch
+        ws_bytes = _workspace_bytes(args)
+        self.workspace = None
+        if ws_bytes:
+            self.workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+            args.workspace, args.workspace_bytes = self.workspace.data_ptr(), ws_bytes
+        args.status = _status_word(device).data_ptr()
+        self._args = args
+        self._args_ref = ctypes.byref(args)
+        self._lib = _native.load()
+        self.kernels = None  # kernels per run, known after the first run
+
+    def run(self):
+        """Enqueue one forward on the current stream; returns the output tensors."""
+        stream = torch.cuda.current_stream(self.device).cuda_stream if DEVICE_TYPE == "cuda" else 0
+        code = self._lib.dsa_sparse_mla_fwd(self._args_ref, stream)
+        if code != _native.STATUS_OK:
+            _native.raise_for_status(code, "dsa_sparse_mla_fwd")
+        self.kernels = self._lib.dsa_last_launch_count()
+        return self.outputs

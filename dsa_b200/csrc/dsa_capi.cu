@@ -84,6 +84,10 @@ int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t leng
       if (bn != 32 && bn != 64) return DSA_STATUS_UNSUPPORTED;
       break;
     }
+    case DSA_FAMILY_STREAM: {
+      if (launch->heads_per_cta != 16 || heads % 16 != 0 || bn != 32) return DSA_STATUS_UNSUPPORTED;
+      break;
+    }
     case DSA_FAMILY_UMMA:
     case DSA_FAMILY_UMMA_PAIR: {
       if (launch->heads_per_cta != 128 || heads != 128 || bn != 32) return DSA_STATUS_UNSUPPORTED;
@@ -123,28 +127,25 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
     if (ctas <= 0) ctas = sm_count();
     const int64_t halves = 2 * batch * queries;
     const int64_t tiles = (topk + 31) / 32;
-    int64_t split = (ctas + halves - 1) / halves;
+    int64_t split = ctas / halves;  // one wave: at most one item per resident CTA
     if (split > tiles) split = tiles;
     if (split < 1) split = 1;
     e.split = (int32_t)split;
     *out = e;
     return DSA_STATUS_OK;
   }
-  e.family = DSA_FAMILY_WARP_MMA;
+  // stream family: persistent CTAs over (token, 16-head group, split)
+  // items; split the TOPK range only until every resident CTA has an item.
+  e.family = DSA_FAMILY_STREAM;
   e.heads_per_cta = 16;
   e.keys_per_tile = 32;
-  // Enough CTAs for two full waves at two CTAs per SM; split the TOPK range
-  // only when the (token, head-group) jobs alone cannot fill the machine,
-  // keeping at least two tiles per split so the gather pipeline has depth.
+  int ctas = dsa::stream_max_ctas();
+  if (ctas <= 0) ctas = 2 * sm_count();
   const int64_t jobs = batch * queries * (heads / 16);
-  const int64_t target = 4LL * sm_count();
   const int64_t tiles = (topk + e.keys_per_tile - 1) / e.keys_per_tile;
-  int64_t split = 1;
-  if (jobs < target) {
-    split = (target + jobs - 1) / jobs;
-    const int64_t cap = tiles / 2 > 0 ? tiles / 2 : 1;
-    if (split > cap) split = cap;
-  }
+  int64_t split = ctas / jobs;  // one wave of items
+  if (split > tiles) split = tiles;
+  if (split < 1) split = 1;
   e.split = (int32_t)split;
   *out = e;
   return DSA_STATUS_OK;
@@ -219,6 +220,7 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
     case DSA_FAMILY_WARP_MMA: err = dsa::launch_fwd_warp_mma(p, s); break;
     case DSA_FAMILY_UMMA: err = dsa::launch_fwd_umma(p, s); break;
     case DSA_FAMILY_UMMA_PAIR: err = dsa::launch_fwd_pair(p, s); break;
+    case DSA_FAMILY_STREAM: err = dsa::launch_fwd_stream(p, s); break;
     default: return DSA_STATUS_UNSUPPORTED;
   }
   if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;

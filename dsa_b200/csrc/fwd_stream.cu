@@ -1,0 +1,387 @@
+// Persistent warp-specialised sparse-MLA forward for 16-head groups (the
+// "stream" family: any H % 16 == 0, BN = 32 selected rows per tile).
+//
+// Built for the shapes where few heads share each gathered row (H = 16 at
+// TP8): the math per row is small, so the kernel is bound by how many
+// gathered bytes are in flight (decode, rows from HBM) or by the L2 gather
+// rate (prefill with an L2-resident KV). Each CTA loops over work items
+// (token, 16-head group, KV split); two gather warps keep its two stages of
+// 32 rows x 1152 B in flight with 16-byte cp.async (validity taken from the
+// original index, dsa/workspace.py:121-128), independently of the compute
+// warps, and two CTAs share an SM.
+//
+// The four compute warps run the reference's per-tile dataflow
+// (dsa/workspace.py:242-318) with warp-level m16n8k16 BF16 MMAs: S = Q.K^T
+// (warp w owns keys 8w..8w+7), masked FP32 online softmax (scale 1/24,
+// invalid index -> -inf), P rounded to BF16, O += P.V (warp w owns latent
+// columns 128w..128w+127, O stays in registers for the item), then the BF16
+// output and stats (split == 1) or FP32 partials for the merge (split > 1,
+// dsa/workspace.py:356-385).
+//
+// Synchronisation: stage full / empty mbarriers between the gather and the
+// compute warps (every wait bounded, reporting through the status word), and
+// a named barrier among the four compute warps only; the compute warps take
+// every named barrier in the same order and leave together when a bounded
+// wait gives up.
+#include "umma_ptx.cuh"
+
+namespace dsa {
+namespace {
+
+using namespace umma;
+
+constexpr int kStHeads = 16;
+constexpr int kStBN = 32;
+constexpr int kStStages = 2;
+constexpr int kStGatherWarps = kStStages;  // gather warp w owns stage w
+constexpr int kStComputeWarps = 4;
+constexpr int kStThreads = 32 * (kStGatherWarps + kStComputeWarps);
+constexpr int kStRow = kDimQK + 8;       // padded smem row (elements): 1168 B, odd multiple of 16 B
+constexpr int kStPRow = kStBN + 8;
+constexpr int kChunks = kDimQK / 8;      // 72 x 16 B per gathered row
+constexpr int kLatChunks = kDimLatent / 8;
+
+struct StSmem {
+  __nv_bfloat16 q[kStHeads * kStRow];
+  __nv_bfloat16 k[kStStages][kStBN * kStRow];
+  __nv_bfloat16 p[kStHeads * kStPRow];
+  float s[kStHeads * kStBN];
+  int ids[kStStages][kStBN];
+  float m[kStHeads];
+  float l[kStHeads];
+  float alpha[kStHeads];
+  unsigned long long full[kStStages];
+  unsigned long long empty[kStStages];
+  int abort;
+  int stop;  // a compute warp's bounded wait gave up: all compute warps leave
+};
+
+struct StItem {
+  int token, hg, sp, batch, kbeg, kend, ntiles;
+};
+
+__device__ __forceinline__ StItem st_item(const FwdParams& p, int item) {
+  const int hgroups = p.heads / kStHeads;
+  StItem it;
+  it.sp = item % p.split;
+  int rest = item / p.split;
+  it.hg = rest % hgroups;
+  it.token = rest / hgroups;
+  it.batch = it.token / p.queries;
+  split_bounds(p.topk, kStBN, p.split, it.sp, &it.kbeg, &it.kend);
+  it.ntiles = (it.kend - it.kbeg + kStBN - 1) / kStBN;
+  return it;
+}
+
+// Position of one tile in this CTA's sequence (items blockIdx.x, +gridDim.x, ...).
+struct StCursor {
+  int item, t;
+  StItem w;
+};
+
+__device__ __forceinline__ void st_advance(const FwdParams& p, int n_items, StCursor& c, int k) {
+  c.t += k;
+  while (c.item < n_items && c.t >= c.w.ntiles) {
+    c.t -= c.w.ntiles;
+    c.item += gridDim.x;
+    if (c.item < n_items) c.w = st_item(p, c.item);
+  }
+}
+
+__device__ __forceinline__ StCursor st_start(const FwdParams& p, int n_items, int k) {
+  StCursor c;
+  c.item = blockIdx.x;
+  c.t = 0;
+  if (c.item < n_items) c.w = st_item(p, c.item);
+  st_advance(p, n_items, c, k);
+  return c;
+}
+
+__device__ __forceinline__ int st_index(const FwdParams& p, const StCursor& c, int n_items, int lane) {
+  if (c.item >= n_items) return -1;
+  const int j = c.w.kbeg + c.t * kStBN + lane;
+  return j < c.w.kend ? __ldg(p.ids + (size_t)c.w.token * p.topk + j) : -1;
+}
+
+__device__ __forceinline__ void compute_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kStComputeWarps) : "memory");
+}
+
+__global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  StSmem& sm = *reinterpret_cast<StSmem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int n_items = p.tokens * (p.heads / kStHeads) * p.split;
+  const int L = p.length;
+  volatile int* abort_flag = &sm.abort;
+  const uint32_t full0 = smem_u32(&sm.full[0]);
+  const uint32_t empty0 = smem_u32(&sm.empty[0]);
+
+  if (tid == 0) {
+    for (int s = 0; s < kStStages; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, kStComputeWarps);
+    }
+    sm.abort = 0;
+    sm.stop = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp < kStGatherWarps) {
+    // ---------------- gather: warp w fills stage w for tiles w, w + 2, ... ----------------
+    const int s = warp;
+    const uint32_t stage = smem_u32(sm.k[s]);
+    const int j8 = lane & 7;  // 16-byte chunk within a 128-byte run
+    const int kq = lane >> 3;  // row within a group of 4
+    StCursor cur = st_start(p, n_items, s);
+    StCursor nx = cur;
+    st_advance(p, n_items, nx, kStStages);
+    StCursor nx2 = nx;
+    st_advance(p, n_items, nx2, kStStages);
+    int idx_cur = st_index(p, cur, n_items, lane);
+    int idx_nx = st_index(p, nx, n_items, lane);
+    uint32_t n = 0;
+    bool ok = true;
+    while (cur.item < n_items) {
+      if (n > 0) {
+        if (lane == 0) ok = mbar_wait(empty0 + 8u * s, (n - 1) & 1u, abort_flag);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+      }
+      sm.ids[s][lane] = idx_cur;  // validity is judged from the original index
+      const int row = min(max(idx_cur, 0), L - 1);
+      const __nv_bfloat16* kv_b = p.kv + (size_t)cur.w.batch * L * kDimLatent;
+      const __nv_bfloat16* kr_b = p.k_rope + (size_t)cur.w.batch * L * kDimRope;
+#pragma unroll 2
+      for (int i = 0; i < kStBN / 4; ++i) {
+        const int key = kq + 4 * i;
+        const int rk = __shfl_sync(0xffffffffu, row, key);
+        const uint32_t dst = stage + (uint32_t)(key * kStRow + j8 * 8) * 2u;
+        const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * 128u, src + kb * 64);
+        cp_async_16(dst + 8u * 128u, kr_b + (size_t)rk * kDimRope + j8 * 8);
+      }
+      cp_async_commit();
+      const int idx_nx2 = st_index(p, nx2, n_items, lane);  // consumed one round later
+      cp_async_wait<0>();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(full0 + 8u * s);
+      ++n;
+      cur = nx;
+      nx = nx2;
+      st_advance(p, n_items, nx2, kStStages);
+      idx_cur = idx_nx;
+      idx_nx = idx_nx2;
+    }
+    if (!ok && lane == 0) report_error(p.status, kErrTimeout);
+    return;
+  }
+
+  // ---------------- compute warps ----------------
+  const int ctid = tid - 32 * kStGatherWarps;  // 0..127
+  const int cw = ctid >> 5;                    // compute warp 0..3
+  const int g = lane >> 2;                     // mma group id (row within 8)
+  const int tq = lane & 3;                     // thread in group
+  constexpr int kKeysPerWarp = kStBN / 4;      // 8 QK keys per warp
+  uint32_t gt = 0;                             // tile counter of this CTA
+  bool failed = false;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const StItem w = st_item(p, item);
+    const int h0 = w.hg * kStHeads;
+    // Q tile [16 heads x (512 | 64)] -> smem; the previous item's readers are done.
+    compute_sync();
+    for (int c = ctid; c < kStHeads * kChunks; c += 32 * kStComputeWarps) {
+      const int r = c / kChunks, part = c % kChunks;
+      const size_t qrow = (size_t)w.token * p.heads + h0 + r;
+      const __nv_bfloat16* src = part < kLatChunks ? p.q + qrow * kDimLatent + part * 8
+                                                   : p.q_rope + qrow * kDimRope + (part - kLatChunks) * 8;
+      cp_async_16(smem_u32(&sm.q[r * kStRow + part * 8]), src);
+    }
+    cp_async_commit();
+    if (ctid < kStHeads) {
+      sm.m[ctid] = kNegFltMax;  // finite start, as dsa/workspace.py:68
+      sm.l[ctid] = 0.f;
+    }
+    cp_async_wait<0>();
+    compute_sync();
+
+    float acc[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+
+    for (int t = 0; t < w.ntiles; ++t, ++gt) {
+      const int s = (int)(gt % kStStages);
+      // stage full: every compute warp waits (bounded), then all agree
+      if (!mbar_wait(full0 + 8u * s, (gt / kStStages) & 1u, abort_flag)) sm.stop = 1;
+      compute_sync();
+      if (*reinterpret_cast<volatile int*>(&sm.stop)) {
+        failed = true;
+        break;
+      }
+
+      // ---- S = Q.K^T for this warp's keys ----
+      {
+        const uint32_t qbase =
+            smem_u32(sm.q) + (((lane & 7) + ((lane >> 3) & 1) * 8) * kStRow + (lane >> 4) * 8) * 2;
+        const int key0 = cw * kKeysPerWarp;
+        const uint32_t kbase = smem_u32(sm.k[s]) + ((key0 + (lane & 7)) * kStRow + (lane >> 3) * 8) * 2;
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 6
+        for (int kp = 0; kp < kDimQK / 32; ++kp) {
+          uint32_t a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3;
+          ldmatrix_x4(qbase + kp * 64, a0, a1, a2, a3);
+          ldmatrix_x4(qbase + kp * 64 + 32, a4, a5, a6, a7);
+          ldmatrix_x4(kbase + kp * 64, b0, b1, b2, b3);
+          mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
+          mma_bf16_16816(d1, a4, a5, a6, a7, b2, b3);
+        }
+        const int col = key0 + tq * 2;
+        const int i0 = sm.ids[s][col], i1 = sm.ids[s][col + 1];
+        const bool v0 = (i0 >= 0) & (i0 < L), v1 = (i1 >= 0) & (i1 < L);
+        const float ninf = -INFINITY;
+        sm.s[g * kStBN + col] = v0 ? __fdiv_rn(d0[0] + d1[0], 24.0f) : ninf;
+        sm.s[g * kStBN + col + 1] = v1 ? __fdiv_rn(d0[1] + d1[1], 24.0f) : ninf;
+        sm.s[(g + 8) * kStBN + col] = v0 ? __fdiv_rn(d0[2] + d1[2], 24.0f) : ninf;
+        sm.s[(g + 8) * kStBN + col + 1] = v1 ? __fdiv_rn(d0[3] + d1[3], 24.0f) : ninf;
+      }
+      compute_sync();
+
+      // ---- online softmax: 8 threads per head row ----
+      {
+        constexpr int kCols = kStBN / 8;
+        const int r = ctid >> 3;
+        const int c0 = (ctid & 7) * kCols;
+        const float m_old = sm.m[r];
+        const float l_old = sm.l[r];
+        __syncwarp();
+        float x[kCols];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) {
+          x[i] = sm.s[r * kStBN + c0 + i];
+          mx = fmaxf(mx, x[i]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const float m_new = fmaxf(m_old, mx);
+        const float alpha = expf(m_old - m_new);
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < kCols; i += 2) {
+          const float p0 = expf(x[i] - m_new);
+          const float p1 = expf(x[i + 1] - m_new);
+          sum += p0 + p1;
+          *reinterpret_cast<uint32_t*>(&sm.p[r * kStPRow + c0 + i]) = pack_bf16x2(p0, p1);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        if ((ctid & 7) == 0) {
+          sm.m[r] = m_new;
+          sm.l[r] = alpha * l_old + sum;
+          sm.alpha[r] = alpha;
+        }
+      }
+      compute_sync();
+
+      // ---- O = alpha*O + P.V over this warp's 128 latent columns ----
+      {
+        const float al0 = sm.alpha[g], al1 = sm.alpha[g + 8];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          acc[j][0] *= al0;
+          acc[j][1] *= al0;
+          acc[j][2] *= al1;
+          acc[j][3] *= al1;
+        }
+        const uint32_t pbase =
+            smem_u32(sm.p) + (((lane & 7) + ((lane >> 3) & 1) * 8) * kStPRow + (lane >> 4) * 8) * 2;
+        const uint32_t vbase = smem_u32(sm.k[s]) +
+                               (((lane & 7) + ((lane >> 3) & 1) * 8) * kStRow + cw * 128 + (lane >> 4) * 8) * 2;
+#pragma unroll
+        for (int kk = 0; kk < kStBN / 16; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(pbase + kk * 32, a0, a1, a2, a3);
+#pragma unroll
+          for (int jp = 0; jp < 8; ++jp) {
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4_trans(vbase + (kk * 16 * kStRow + jp * 16) * 2, b0, b1, b2, b3);
+            mma_bf16_16816(acc[2 * jp], a0, a1, a2, a3, b0, b1);
+            mma_bf16_16816(acc[2 * jp + 1], a0, a1, a2, a3, b2, b3);
+          }
+        }
+      }
+      // this warp is done with stage s
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8u * s);
+    }
+    if (failed) break;
+
+    // ---- epilogue (sm.m / sm.l final after the last softmax barrier) ----
+    const float l0 = sm.l[g], l1 = sm.l[g + 8];
+    if (p.split == 1) {
+      __nv_bfloat16* o0 = p.out + ((size_t)w.token * p.heads + h0 + g) * kDimLatent + cw * 128 + tq * 2;
+      __nv_bfloat16* o1 = o0 + 8 * kDimLatent;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        *reinterpret_cast<uint32_t*>(o0 + j * 8) = pack_bf16x2(__fdiv_rn(acc[j][0], l0), __fdiv_rn(acc[j][1], l0));
+        *reinterpret_cast<uint32_t*>(o1 + j * 8) = pack_bf16x2(__fdiv_rn(acc[j][2], l1), __fdiv_rn(acc[j][3], l1));
+      }
+      if (ctid < kStHeads) {
+        p.out_max[(size_t)w.token * p.heads + h0 + ctid] = sm.m[ctid];
+        p.out_sum[(size_t)w.token * p.heads + h0 + ctid] = sm.l[ctid];
+      }
+    } else {
+      const size_t prow = ((size_t)w.token * p.split + w.sp) * p.heads + h0;
+      float* n0 = p.part_num + (prow + g) * kDimLatent + cw * 128 + tq * 2;
+      float* n1 = n0 + 8 * kDimLatent;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        *reinterpret_cast<float2*>(n0 + j * 8) = make_float2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<float2*>(n1 + j * 8) = make_float2(acc[j][2], acc[j][3]);
+      }
+      if (ctid < kStHeads) {
+        p.part_max[prow + ctid] = sm.m[ctid];
+        p.part_sum[prow + ctid] = sm.l[ctid];
+      }
+    }
+  }
+  if (failed && ctid == 0) report_error(p.status, kErrTimeout);
+}
+
+}  // namespace
+
+int stream_max_ctas() {
+  static int cached = -1;
+  if (cached > 0) return cached;
+  const int smem = (int)sizeof(StSmem);
+  if (cudaFuncSetAttribute(fwd_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return -1;
+  int per_sm = 0, dev = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_stream_kernel, kStThreads, smem) != cudaSuccess ||
+      per_sm <= 0)
+    return -1;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return -1;
+  cached = per_sm * sms;
+  return cached;
+}
+
+cudaError_t launch_fwd_stream(const FwdParams& p, cudaStream_t stream) {
+  if (p.heads % kStHeads != 0 || p.keys_per_tile != kStBN) return cudaErrorInvalidValue;
+  const int max_ctas = stream_max_ctas();
+  if (max_ctas <= 0) return cudaErrorInvalidConfiguration;
+  const long long items = (long long)p.tokens * (p.heads / kStHeads) * p.split;
+  if (items <= 0 || items > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const int ctas = (int)(items < max_ctas ? items : max_ctas);
+  fwd_stream_kernel<<<ctas, kStThreads, sizeof(StSmem), stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace dsa

@@ -348,28 +348,38 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       {
         const size_t qrow = (size_t)w.token * kUmHeads + row;
         const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
-#pragma unroll 1
+        // dims 320..511 and the rope dims -> shared memory, asynchronously
+        const uint32_t qdst = base + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
+#pragma unroll
+        for (int k = 0; k < (kDimLatent - kQTmemDims) / 8; ++k)  // latent dims 320..511: 3 blocks
+          cp_async_16(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16), src + kQTmemDims / 8 + k);
+        const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) cp_async_16(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16), rsrc + k);
+        cp_async_commit();
+        // dims 0..319 -> TMEM, the next chunk's loads in flight while one is stored
+        uint4 qa[8], qb[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) qa[k] = __ldg(src + k);
+#pragma unroll
         for (int ch = 0; ch < kQTmemDims / 64; ++ch) {
+          if (ch + 1 < kQTmemDims / 64) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) qb[k] = __ldg(src + (ch + 1) * 8 + k);
+          }
           uint32_t r[32];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const uint4 v = __ldg(src + ch * 8 + k);
-            r[4 * k] = v.x;
-            r[4 * k + 1] = v.y;
-            r[4 * k + 2] = v.z;
-            r[4 * k + 3] = v.w;
+            r[4 * k] = qa[k].x;
+            r[4 * k + 1] = qa[k].y;
+            r[4 * k + 2] = qa[k].z;
+            r[4 * k + 3] = qa[k].w;
           }
           tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) qa[k] = qb[k];
         }
-        uint8_t* const qdst = sbase + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
-#pragma unroll
-        for (int k = 0; k < (kDimLatent - kQTmemDims) / 8; ++k)  // latent dims 320..511: 3 blocks
-          *reinterpret_cast<uint4*>(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16)) =
-              __ldg(src + kQTmemDims / 8 + k);
-        const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<uint4*>(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16)) = __ldg(rsrc + k);
+        cp_async_wait<0>();
         fence_proxy_async_smem();
         tmem_wait_st();
         tc_fence_before();

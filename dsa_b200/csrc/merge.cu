@@ -2,45 +2,93 @@
 //
 // For one (token, head): m = max_s m_s, w_s = exp(m_s - m),
 // l = sum_s w_s l_s, o = sum_s w_s u_s / l -> BF16, stats (m, l).
-// One 128-thread group per (token, head), each thread owning 4 consecutive
-// latent columns, so every partial row is read once with 16-byte loads.
+// One block per (token, head): kMergeGroups groups of 128 threads, each
+// thread owning 4 consecutive latent columns, so every partial row is read
+// once with 16-byte loads. The split statistics are reduced across lanes;
+// group g sums the numerators of splits 8g..8g+7, 8g+32.. (kMergeUnroll rows
+// in flight per thread) and the groups are added through shared memory.
 #include "dsa_common.cuh"
 
 namespace dsa {
 namespace {
 
-constexpr int kMergeHeadsPerBlock = 2;
-constexpr int kMergeThreads = 128 * kMergeHeadsPerBlock;
+constexpr int kMergeGroups = 4;                  // thread groups per (token, head), each over 1/4 of the splits
+constexpr int kMergeThreads = 128 * kMergeGroups; // a group's thread owns 4 consecutive columns
+constexpr int kMergeUnroll = 8;                  // partial rows in flight per thread
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(
     const float* __restrict__ num, const float* __restrict__ pmax,
     const float* __restrict__ psum, __nv_bfloat16* __restrict__ out,
     float* __restrict__ omax, float* __restrict__ osum, int tokens, int heads, int split) {
-  const long long th = (long long)blockIdx.x * kMergeHeadsPerBlock + (threadIdx.x >> 7);
-  if (th >= (long long)tokens * heads) return;
+  __shared__ float4 acc[kMergeGroups - 1][128];
+  const long long th = blockIdx.x;
   const int t = (int)(th / heads), h = (int)(th % heads);
+  const int lane = threadIdx.x & 31;
+  const int grp = threadIdx.x >> 7;
   const int c = (threadIdx.x & 127) * 4;
   const size_t stat0 = (size_t)t * split * heads + h;  // + s*heads
 
+  // split statistics: lanes take splits lane, lane+32, ... (every warp computes them)
   float m = -INFINITY;
-  for (int s = 0; s < split; ++s) m = fmaxf(m, __ldg(pmax + stat0 + (size_t)s * heads));
+  for (int s = lane; s < split; s += 32) m = fmaxf(m, __ldg(pmax + stat0 + (size_t)s * heads));
+  m = warp_max(m);
   float l = 0.f;
+  for (int s = lane; s < split; s += 32)
+    l += expf(__ldg(pmax + stat0 + (size_t)s * heads) - m) * __ldg(psum + stat0 + (size_t)s * heads);
+  l = warp_sum(l);
+
+  // numerator over this group's splits, kMergeUnroll 16-byte loads in flight per thread
   float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s = 0; s < split; ++s) {
-    const float w = expf(__ldg(pmax + stat0 + (size_t)s * heads) - m);
-    l += w * __ldg(psum + stat0 + (size_t)s * heads);
-    const float4 v = __ldg(reinterpret_cast<const float4*>(
-        num + (stat0 + (size_t)s * heads) * kDimLatent + c));
-    u.x += w * v.x;
-    u.y += w * v.y;
-    u.z += w * v.z;
-    u.w += w * v.w;
+  for (int s0 = grp * kMergeUnroll; s0 < split; s0 += kMergeGroups * kMergeUnroll) {
+    float4 v[kMergeUnroll];
+    float w[kMergeUnroll];
+#pragma unroll
+    for (int j = 0; j < kMergeUnroll; ++j) {
+      const int s = s0 + j;
+      if (s < split) {
+        v[j] = __ldg(reinterpret_cast<const float4*>(num + (stat0 + (size_t)s * heads) * kDimLatent + c));
+        w[j] = __ldg(pmax + stat0 + (size_t)s * heads);
+      } else {
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        w[j] = -INFINITY;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kMergeUnroll; ++j) {
+      const float ww = expf(w[j] - m);
+      u.x += ww * v[j].x;
+      u.y += ww * v[j].y;
+      u.z += ww * v[j].z;
+      u.w += ww * v[j].w;
+    }
+  }
+  if (grp > 0) acc[grp - 1][threadIdx.x & 127] = u;
+  __syncthreads();
+  if (grp != 0) return;
+#pragma unroll
+  for (int g = 0; g < kMergeGroups - 1; ++g) {
+    const float4 o = acc[g][threadIdx.x];
+    u.x += o.x;
+    u.y += o.y;
+    u.z += o.z;
+    u.w += o.w;
   }
   uint2 packed;
   packed.x = pack_bf16x2(__fdiv_rn(u.x, l), __fdiv_rn(u.y, l));
   packed.y = pack_bf16x2(__fdiv_rn(u.z, l), __fdiv_rn(u.w, l));
   *reinterpret_cast<uint2*>(out + (size_t)th * kDimLatent + c) = packed;
-  if (c == 0) {
+  if (threadIdx.x == 0) {
     omax[th] = m;
     osum[th] = l;
   }
@@ -51,8 +99,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(
 cudaError_t launch_merge(const float* num, const float* pmax, const float* psum,
                          __nv_bfloat16* out, float* omax, float* osum, int tokens, int heads,
                          int split, cudaStream_t stream) {
-  const long long pairs = (long long)tokens * heads;
-  const long long blocks = (pairs + kMergeHeadsPerBlock - 1) / kMergeHeadsPerBlock;
+  const long long blocks = (long long)tokens * heads;
   if (blocks <= 0 || blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   merge_kernel<<<(unsigned)blocks, kMergeThreads, 0, stream>>>(num, pmax, psum, out, omax, osum,
                                                               tokens, heads, split);

@@ -67,8 +67,10 @@ typedef enum dsa_family {
   DSA_FAMILY_WARP_MMA = 1,  /* generic: 16 heads per CTA, warp-level MMA, any H % 16 == 0 */
   DSA_FAMILY_UMMA = 2,      /* tcgen05/TMEM path, H == 128: one CTA per (query, half of the 512
                                value columns); each CTA computes the full scores */
-  DSA_FAMILY_UMMA_PAIR = 3  /* tcgen05/TMEM path, H == 128: a 2-CTA cluster per query, one CTA
+  DSA_FAMILY_UMMA_PAIR = 3, /* tcgen05/TMEM path, H == 128: a 2-CTA cluster per query, one CTA
                                computes scores + softmax, the other P.V over all 512 columns */
+  DSA_FAMILY_STREAM = 4     /* persistent warp-level MMA, 16 heads per CTA item, gather warps keep
+                               the selected rows in flight; any H % 16 == 0, keys_per_tile 32 */
 } dsa_family_t;
 
 /* One entry of the shape-keyed launch table (reference: Tuning,
