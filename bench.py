@@ -52,9 +52,9 @@ DEFAULT_CONFIG = "prefill_h128"
 # dram__bytes_write.sum) from the ncu captures summarised under profiles/;
 # None until a capture of that kernel/config exists.
 TRAFFIC_BYTES = {
-    # profiles/fwd_umma_prefill_h128.md: 398.6 MB for a 512-query capture of
-    # fwd_umma_kernel, scaled to 16384 queries.
-    "prefill_h128": int(398.6e6 * 16384 / 512),
+    # profiles/fwd_pair_prefill_h128.md: 394.4 MB (DRAM read + write) for a
+    # 512-query capture of fwd_pair_kernel, scaled to 16384 queries.
+    "prefill_h128": int(394.4e6 * 16384 / 512),
 }
 
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
@@ -314,6 +314,9 @@ def main():
     ap.add_argument("--shape", default=None,
                     help="B,SQ,H,L,TOPK override (a reduced case for profiling; workload 'custom')")
     ap.add_argument("--variant", default="uniform", choices=("uniform", "peaked", "duplicates"))
+    ap.add_argument("--tuning", default=None,
+                    help="bm,bn,split[,pv_cols] launch entry instead of the shape-keyed default "
+                         "(selects a kernel family, e.g. 128,32,1,256 for the split-V family)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -345,7 +348,11 @@ def main():
     # The timed step replays a CUDA graph of the prepared forward (checks and
     # allocations done once, as a serving loop does); `e2e` below goes through
     # dsa_b200.forward with host copies every step.
-    plans = [dsa_b200.ForwardPlan(*v) for v in views]
+    tuning = None
+    if args.tuning:
+        f = [int(v) for v in args.tuning.split(",")]
+        tuning = dsa_b200.Tuning(f[0], f[1], f[2], pv_cols=f[3] if len(f) > 3 else 512)
+    plans = [dsa_b200.ForwardPlan(*v, config=tuning) for v in views]
     for pl in plans:
         pl.run()
     torch.cuda.synchronize()
@@ -409,7 +416,7 @@ def main():
             ddst.copy_(hsrc, non_blocking=True)
         vws = [(dev_in[0][b0:b1, s0:s1], dev_in[1][b0:b1], dev_in[2][b0:b1, s0:s1], dev_in[3][b0:b1],
                 dev_in[4][b0:b1, s0:s1]) for b0, b1, s0, s1 in pieces]
-        outs = [dsa_b200.forward(*v) for v in vws]
+        outs = [dsa_b200.forward(*v, config=tuning) for v in vws]
         if out_host is None:
             out_host = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in o] for o in outs]
         for o, hdst in zip(outs, out_host):
@@ -441,7 +448,9 @@ def main():
     rank_share = (hi - lo) / (b * s)
     per_launch_flops = flops * rank_share
     per_launch_bytes = gathered * rank_share
-    if h >= 64:
+    # Decode shapes are judged on gathered bytes against HBM, prefill shapes
+    # (many queries per call) on FLOPs against the BF16 tensor peak.
+    if s >= 64 or (args.config.startswith("prefill")):
         bound, achieved, peak, unit = "tensor", per_launch_flops / (ms_per_step * 1e-3) / 1e12, tf_peak, "TFLOP/s"
     else:
         bound, achieved, peak, unit = "hbm", per_launch_bytes / (ms_per_step * 1e-3) / 1e9, hbm_peak, "GB/s"
@@ -463,7 +472,8 @@ def main():
                    "index_variant": args.variant, "seed": SEED,
                    "parallelism": f"query-shard x{world}, kv replicated",
                    "l2": "flushed between timed iterations (256 MiB write outside the events)",
-                   "timed": "CUDA-graph replay of ForwardPlan.run (one graph per step)"},
+                   "timed": "CUDA-graph replay of ForwardPlan.run (one graph per step)",
+                   "launch": {"family": int(plans[0].launch.family), "split": int(plans[0].launch.split)}},
         "calls_per_s": 1e6 / us,
         "tflops": flops / (us * 1e-6) / 1e12,
         "gathered_gbs": gathered / (us * 1e-6) / 1e9,

@@ -7,17 +7,19 @@ reference results (the rule of dsa/config.py:3).
 that existing callers can still pass ``config=Tuning(...)``. Their meaning on
 B200:
 
-* ``bm`` — heads that share one gathered KV tile. ``bm == 128`` selects the
-  tcgen05/TMEM family (one 2-CTA cluster per query for H = 128) once that
-  family is built; any other legal ``bm`` selects the generic warp-MMA family,
-  whose CTAs each own 16 heads.
-* ``bn`` — selected KV rows per pipeline stage (32 or 64 for warp-MMA).
+* ``bm`` — heads that share one gathered KV tile. ``bm == 128`` selects a
+  tcgen05/TMEM family for H = 128; any other legal ``bm`` selects a 16-head
+  family (each CTA item owns 16 heads).
+* ``bn`` — selected KV rows per pipeline stage: 32 (tcgen05 families and the
+  persistent stream family for ``bm < 128``) or 64 (the warp-MMA family).
 * ``split`` — KV splits per (query, head tile); ``split > 1`` writes FP32
   partials to the workspace and runs the FP32 merge (dsa/merge.py).
-* ``direct_nz``, ``pv_cols``, ``share_score`` — Ascend data-movement knobs
-  (NZ packing, PV fragment width, score/PV UB sharing) with no counterpart on
-  sm_100a. They are type-checked as in the reference but do not change the
-  launch.
+* ``pv_cols`` — value columns one CTA accumulates, for ``bm == 128``: 512
+  selects the pair family (score CTA + value CTA per query), 256 the split-V
+  family (two CTAs per query, each over half of the 512 columns).
+* ``direct_nz``, ``share_score`` — Ascend data-movement knobs (NZ packing,
+  score/PV UB sharing) with no counterpart on sm_100a. They are type-checked
+  as in the reference but do not change the launch.
 
 ``CASE_SHAPES`` holds the reference's 16 shapes (dsa/config.py:23-40) and the
 five benchmark configs of this build. ``SELECTED`` maps every name to the

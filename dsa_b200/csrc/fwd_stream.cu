@@ -12,7 +12,10 @@
 //
 // The four compute warps run the reference's per-tile dataflow
 // (dsa/workspace.py:242-318) with warp-level m16n8k16 BF16 MMAs: S = Q.K^T
-// (warp w owns keys 8w..8w+7), masked FP32 online softmax (scale 1/24,
+// (warp w owns dims 144w..144w+143 for all 32 keys and keeps its Q slice in
+// registers for the whole item; the four partial scores are added in shared
+// memory, so Q is read from shared memory once per item and every gathered
+// element once per tile), masked FP32 online softmax (scale 1/24,
 // invalid index -> -inf), P rounded to BF16, O += P.V (warp w owns latent
 // columns 128w..128w+127, O stays in registers for the item), then the BF16
 // output and stats (split == 1) or FP32 partials for the merge (split > 1,
@@ -20,9 +23,9 @@
 //
 // Synchronisation: stage full / empty mbarriers between the gather and the
 // compute warps (every wait bounded, reporting through the status word), and
-// a named barrier among the four compute warps only; the compute warps take
-// every named barrier in the same order and leave together when a bounded
-// wait gives up.
+// a named barrier among the four compute warps only (two per tile); the
+// compute warps take every named barrier in the same order and leave
+// together, after the tile's last barrier, when a bounded wait gives up.
 #include "umma_ptx.cuh"
 
 namespace dsa {
@@ -45,7 +48,7 @@ struct StSmem {
   __nv_bfloat16 q[kStHeads * kStRow];
   __nv_bfloat16 k[kStStages][kStBN * kStRow];
   __nv_bfloat16 p[kStHeads * kStPRow];
-  float s[kStHeads * kStBN];
+  float s[kStComputeWarps][kStHeads * kStBN];  // partial scores of each compute warp's dims
   int ids[kStStages][kStBN];
   float m[kStHeads];
   float l[kStHeads];
@@ -101,6 +104,14 @@ __device__ __forceinline__ int st_index(const FwdParams& p, const StCursor& c, i
   if (c.item >= n_items) return -1;
   const int j = c.w.kbeg + c.t * kStBN + lane;
   return j < c.w.kend ? __ldg(p.ids + (size_t)c.w.token * p.topk + j) : -1;
+}
+
+// 2^x on the special-function unit (flushes results below 2^-126 to zero,
+// far below what the FP32 row sums can resolve).
+__device__ __forceinline__ float ex2f_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void compute_sync() {
@@ -208,6 +219,15 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
     }
     cp_async_wait<0>();
     compute_sync();
+    // this warp's Q slice (dims 144cw..144cw+143) as m16n8k16 A fragments
+    constexpr int kQkSteps = kDimQK / 16 / kStComputeWarps;  // 9
+    uint32_t qf[kQkSteps][4];
+    {
+      const uint32_t qbase = smem_u32(sm.q) +
+                             (((lane & 7) + ((lane >> 3) & 1) * 8) * kStRow + (lane >> 4) * 8 + cw * 16 * kQkSteps) * 2;
+#pragma unroll
+      for (int ks = 0; ks < kQkSteps; ++ks) ldmatrix_x4(qbase + ks * 32, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+    }
 
     float acc[16][4];
 #pragma unroll
@@ -215,43 +235,48 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
 
     for (int t = 0; t < w.ntiles; ++t, ++gt) {
       const int s = (int)(gt % kStStages);
-      // stage full: every compute warp waits (bounded), then all agree
+      // stage full: every compute warp waits (bounded); a warp that gives up
+      // flags it and still takes this tile's barriers, and all leave after
+      // the last one
       if (!mbar_wait(full0 + 8u * s, (gt / kStStages) & 1u, abort_flag)) sm.stop = 1;
-      compute_sync();
-      if (*reinterpret_cast<volatile int*>(&sm.stop)) {
-        failed = true;
-        break;
-      }
 
-      // ---- S = Q.K^T for this warp's keys ----
+      // ---- partial S = Q.K^T over this warp's dims, all 32 keys ----
       {
-        const uint32_t qbase =
-            smem_u32(sm.q) + (((lane & 7) + ((lane >> 3) & 1) * 8) * kStRow + (lane >> 4) * 8) * 2;
-        const int key0 = cw * kKeysPerWarp;
-        const uint32_t kbase = smem_u32(sm.k[s]) + ((key0 + (lane & 7)) * kStRow + (lane >> 3) * 8) * 2;
-        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 6
-        for (int kp = 0; kp < kDimQK / 32; ++kp) {
-          uint32_t a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3;
-          ldmatrix_x4(qbase + kp * 64, a0, a1, a2, a3);
-          ldmatrix_x4(qbase + kp * 64 + 32, a4, a5, a6, a7);
-          ldmatrix_x4(kbase + kp * 64, b0, b1, b2, b3);
-          mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
-          mma_bf16_16816(d1, a4, a5, a6, a7, b2, b3);
+        float d[kStBN / 8][4];
+#pragma unroll
+        for (int nt = 0; nt < kStBN / 8; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+        // ldmatrix_x4 over 8 keys x 32 dims: b0,b1 = k-step 2j, b2,b3 = k-step 2j+1
+        const uint32_t kbase =
+            smem_u32(sm.k[s]) + ((lane & 7) * kStRow + (lane >> 3) * 8 + cw * 16 * kQkSteps) * 2;
+#pragma unroll
+        for (int nt = 0; nt < kStBN / 8; ++nt) {
+#pragma unroll
+          for (int j = 0; j < kQkSteps / 2; ++j) {
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4(kbase + (nt * 8 * kStRow + j * 32) * 2, b0, b1, b2, b3);
+            mma_bf16_16816(d[nt], qf[2 * j][0], qf[2 * j][1], qf[2 * j][2], qf[2 * j][3], b0, b1);
+            mma_bf16_16816(d[nt], qf[2 * j + 1][0], qf[2 * j + 1][1], qf[2 * j + 1][2], qf[2 * j + 1][3], b2, b3);
+          }
+          // odd step count: the last 16 dims with an x2 load (8 keys x 16 dims)
+          uint32_t b0, b1;
+          ldmatrix_x2(kbase + (nt * 8 * kStRow + (kQkSteps - 1) * 16) * 2, b0, b1);
+          mma_bf16_16816(d[nt], qf[kQkSteps - 1][0], qf[kQkSteps - 1][1], qf[kQkSteps - 1][2],
+                         qf[kQkSteps - 1][3], b0, b1);
         }
-        const int col = key0 + tq * 2;
-        const int i0 = sm.ids[s][col], i1 = sm.ids[s][col + 1];
-        const bool v0 = (i0 >= 0) & (i0 < L), v1 = (i1 >= 0) & (i1 < L);
-        const float ninf = -INFINITY;
-        sm.s[g * kStBN + col] = v0 ? __fdiv_rn(d0[0] + d1[0], 24.0f) : ninf;
-        sm.s[g * kStBN + col + 1] = v1 ? __fdiv_rn(d0[1] + d1[1], 24.0f) : ninf;
-        sm.s[(g + 8) * kStBN + col] = v0 ? __fdiv_rn(d0[2] + d1[2], 24.0f) : ninf;
-        sm.s[(g + 8) * kStBN + col + 1] = v1 ? __fdiv_rn(d0[3] + d1[3], 24.0f) : ninf;
+        float* const sp = sm.s[cw];
+#pragma unroll
+        for (int nt = 0; nt < kStBN / 8; ++nt) {
+          const int col = nt * 8 + tq * 2;
+          *reinterpret_cast<float2*>(&sp[g * kStBN + col]) = make_float2(d[nt][0], d[nt][1]);
+          *reinterpret_cast<float2*>(&sp[(g + 8) * kStBN + col]) = make_float2(d[nt][2], d[nt][3]);
+        }
       }
       compute_sync();
 
       // ---- online softmax: 8 threads per head row ----
       {
+        // raw (unscaled) scores; exp(s / 24 - m) = 2^(s * c - m * c) with c = log2(e) / 24
+        constexpr float c = 1.4426950408889634f / 24.0f;
         constexpr int kCols = kStBN / 8;
         const int r = ctid >> 3;
         const int c0 = (ctid & 7) * kCols;
@@ -262,19 +287,24 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
         float mx = -INFINITY;
 #pragma unroll
         for (int i = 0; i < kCols; ++i) {
-          x[i] = sm.s[r * kStBN + c0 + i];
+          const int col = c0 + i;
+          const float sc = sm.s[0][r * kStBN + col] + sm.s[1][r * kStBN + col] + sm.s[2][r * kStBN + col] +
+                           sm.s[3][r * kStBN + col];
+          const int id = sm.ids[s][col];
+          x[i] = ((id >= 0) & (id < L)) ? sc : -INFINITY;
           mx = fmaxf(mx, x[i]);
         }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         const float m_new = fmaxf(m_old, mx);
-        const float alpha = expf(m_old - m_new);
+        const float alpha = m_new == m_old ? 1.f : ex2f_approx((m_old - m_new) * c);
+        const float mc = m_new * c;
         float sum = 0.f;
 #pragma unroll
         for (int i = 0; i < kCols; i += 2) {
-          const float p0 = expf(x[i] - m_new);
-          const float p1 = expf(x[i + 1] - m_new);
+          const float p0 = ex2f_approx(fmaf(x[i], c, -mc));
+          const float p1 = ex2f_approx(fmaf(x[i + 1], c, -mc));
           sum += p0 + p1;
           *reinterpret_cast<uint32_t*>(&sm.p[r * kStPRow + c0 + i]) = pack_bf16x2(p0, p1);
         }
@@ -292,12 +322,14 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
       // ---- O = alpha*O + P.V over this warp's 128 latent columns ----
       {
         const float al0 = sm.alpha[g], al1 = sm.alpha[g + 8];
+        if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {  // a row max grew
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          acc[j][0] *= al0;
-          acc[j][1] *= al0;
-          acc[j][2] *= al1;
-          acc[j][3] *= al1;
+          for (int j = 0; j < 16; ++j) {
+            acc[j][0] *= al0;
+            acc[j][1] *= al0;
+            acc[j][2] *= al1;
+            acc[j][3] *= al1;
+          }
         }
         const uint32_t pbase =
             smem_u32(sm.p) + (((lane & 7) + ((lane >> 3) & 1) * 8) * kStPRow + (lane >> 4) * 8) * 2;
@@ -319,6 +351,10 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
       // this warp is done with stage s
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8u * s);
+      if (*reinterpret_cast<volatile int*>(&sm.stop)) {  // set before the softmax barrier
+        failed = true;
+        break;
+      }
     }
     if (failed) break;
 
@@ -333,7 +369,8 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
         *reinterpret_cast<uint32_t*>(o1 + j * 8) = pack_bf16x2(__fdiv_rn(acc[j][2], l1), __fdiv_rn(acc[j][3], l1));
       }
       if (ctid < kStHeads) {
-        p.out_max[(size_t)w.token * p.heads + h0 + ctid] = sm.m[ctid];
+        const float mr = sm.m[ctid];
+        p.out_max[(size_t)w.token * p.heads + h0 + ctid] = mr == kNegFltMax ? mr : __fdiv_rn(mr, 24.0f);
         p.out_sum[(size_t)w.token * p.heads + h0 + ctid] = sm.l[ctid];
       }
     } else {
@@ -346,7 +383,8 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
         *reinterpret_cast<float2*>(n1 + j * 8) = make_float2(acc[j][2], acc[j][3]);
       }
       if (ctid < kStHeads) {
-        p.part_max[prow + ctid] = sm.m[ctid];
+        const float mr = sm.m[ctid];
+        p.part_max[prow + ctid] = mr == kNegFltMax ? mr : __fdiv_rn(mr, 24.0f);
         p.part_sum[prow + ctid] = sm.l[ctid];
       }
     }
