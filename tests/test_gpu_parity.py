@@ -142,15 +142,17 @@ def test_split_invariance_full_size(cuda_lib):
     assert m["denominator"]["max_normalized"] < 1e-5, m
 
 
-def test_merge_entry_point(cuda_lib):
-    t, s, h = 5, 4, 32
+@pytest.mark.parametrize("s", [1, 4, 5, 16, 17, 40])  # warp-per-row kernel up to 16 splits, block kernel above
+def test_merge_entry_point(cuda_lib, s):
+    t, h = 5, 32
     g = torch.Generator().manual_seed(1)
     num = torch.randn((t, s, h, 512), generator=g)
     pm = torch.randn((t, s, h), generator=g) * 3
-    pm[1, 2] = oracle.FLT_MAX * -1  # an all-masked split merges with weight 0
     pl = torch.rand((t, s, h), generator=g) * 50 + 1
-    pl[1, 2] = 0
-    num[1, 2] = 0
+    if s > 2:
+        pm[1, 2] = oracle.FLT_MAX * -1  # an all-masked split merges with weight 0
+        pl[1, 2] = 0
+        num[1, 2] = 0
     ref = oracle.merge_partials(num, pm, pl)
     dn, dm, dl = num.cuda(), pm.cuda(), pl.cuda()
     out = torch.empty((t, h, 512), dtype=torch.bfloat16, device="cuda")
