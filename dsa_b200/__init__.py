@@ -5,5 +5,7 @@ Drop-in for ``dsa.forward`` (dsa/__init__.py:2-5 of the reference):
 """
 from .api import ForwardPlan, device_status, forward
 from .config import CASE_SHAPES, SELECTED, Tuning
+from .sparse_flash_attention import npu_sparse_flash_attention, sparse_flash_attention
 
-__all__ = ["forward", "ForwardPlan", "Tuning", "CASE_SHAPES", "SELECTED", "device_status"]
+__all__ = ["forward", "ForwardPlan", "Tuning", "CASE_SHAPES", "SELECTED", "device_status",
+           "sparse_flash_attention", "npu_sparse_flash_attention"]

@@ -10,7 +10,7 @@ import ctypes
 import os
 import threading
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libdsa_b200.so")
 
 STATUS_OK = 0
@@ -60,6 +60,7 @@ class FwdArgs(ctypes.Structure):
         ("launch", Launch),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
         ("status", ctypes.c_void_p),
+        ("scale", ctypes.c_float),
     ]
 
 

@@ -58,6 +58,23 @@ def _check_cores(cores):
         raise ValueError("cores must be a positive int")
 
 
+SCALE_MAX = 0.5
+
+
+def _check_scale(scale):
+    """``None`` keeps the reference's fixed 1/sqrt(576) = 1/24 (0.0 at the C
+    ABI); otherwise a real number in (0, 0.5] (every 1/sqrt(d) with d >= 4;
+    larger scales would overflow the kernels' masked-key arithmetic)."""
+    if scale is None:
+        return 0.0
+    if isinstance(scale, bool) or not isinstance(scale, (int, float)):
+        raise ValueError("scale must be None or a float")
+    value = float(scale)
+    if not (0.0 < value <= SCALE_MAX):
+        raise ValueError(f"scale must be in (0, {SCALE_MAX}], got {value}")
+    return value
+
+
 def _check_tuning(config, shape, cores):
     """Launch-entry checks: the reference's field rules (dsa/api.py:46-65)
     plus what the sm_100a kernels support (dsa_check_launch)."""
@@ -138,14 +155,19 @@ def _workspace_bytes(args):
     return int(_native.load().dsa_fwd_workspace_bytes(ctypes.byref(args)))
 
 
-def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_kernels=False):
+def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_kernels=False,
+            scale=None):
     """Sparse MLA attention with given top-k indices.
 
     Returns ``(output, softmax_max, softmax_sum)``: output BF16
     ``[B,SQ,H,512]``; the two statistics FP32 ``[B,1,SQ,H]`` (natural-exp
-    max and sum of the scaled scores). The scale is fixed at 1/sqrt(512+64).
+    max and sum of the scaled scores). The scale is the reference's fixed
+    1/sqrt(512+64) unless ``scale`` gives one in (0, 0.5] (the reference
+    fixes 1/24 and notes that a model keeps its own scale, README.md:81-84).
     Duplicate indices keep their repeated weight; indices outside [0, L) are
-    masked. Every query needs at least one valid index (dsa/api.py:82-91).
+    masked. The reference requires at least one valid index per query
+    (dsa/api.py:82-91); here a (query, head) row without one gets output 0,
+    softmax_max -inf and softmax_sum 0.
 
     ``config`` overrides the shape-keyed launch entry; ``cores`` is validated
     for compatibility; ``return_kernels=True`` returns
@@ -153,6 +175,7 @@ def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_ker
     Work is enqueued on ``torch.cuda.current_stream()``; nothing synchronises.
     """
     shape, device = _check_inputs(q, kv, q_rope, k_rope, indices)
+    scale_arg = _check_scale(scale)
     if config is None:
         _check_cores(cores)
         launch = _default_launch(shape, device)
@@ -171,6 +194,7 @@ def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_ker
     args.output, args.softmax_max, args.softmax_sum = output.data_ptr(), maximum.data_ptr(), denominator.data_ptr()
     args.batch, args.queries, args.heads, args.length, args.topk = shape
     args.launch = launch
+    args.scale = scale_arg
     ws_bytes = _workspace_bytes(args)
     workspace = None
     if ws_bytes:
@@ -202,8 +226,9 @@ class ForwardPlan:
     ``(output, softmax_max, softmax_sum)`` tensors every run.
     """
 
-    def __init__(self, q, kv, q_rope, k_rope, indices, *, config=None, cores=28):
+    def __init__(self, q, kv, q_rope, k_rope, indices, *, config=None, cores=28, scale=None):
         shape, device = _check_inputs(q, kv, q_rope, k_rope, indices)
+        scale_arg = _check_scale(scale)
         if config is None:
             _check_cores(cores)
             launch = _default_launch(shape, device)
@@ -223,6 +248,7 @@ class ForwardPlan:
         args.output, args.softmax_max, args.softmax_sum = (t.data_ptr() for t in self.outputs)
         args.batch, args.queries, args.heads, args.length, args.topk = shape
         args.launch = launch
+        args.scale = scale_arg
         ws_bytes = _workspace_bytes(args)
         self.workspace = None
         if ws_bytes:

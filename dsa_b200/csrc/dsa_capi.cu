@@ -213,6 +213,7 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
   p.split = e.split;
   p.keys_per_tile = e.keys_per_tile;
   p.heads_per_cta = e.heads_per_cta;
+  if (!dsa::fill_scale(a->scale, p)) return DSA_STATUS_BAD_ARGUMENT;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err = cudaSuccess;

@@ -44,7 +44,34 @@ struct FwdParams {
   int split;
   int keys_per_tile;
   int heads_per_cta;
+  // Scores are divided by scale_div (= 1/scale; exactly 24 for the
+  // reference's 1/sqrt(576)); the exp2-form families use
+  // scale_log2 = log2(e) / scale_div.
+  float scale_div;
+  float scale_log2;
 };
+
+// Host: fill scale_div / scale_log2 from the ABI's scale (0 = the
+// reference's 1/sqrt(576), divisor exactly 24; otherwise (0, 0.5], which
+// keeps -FLT_MAX * scale_log2 finite for the masked-key arithmetic).
+// Returns false for a scale outside that range.
+inline bool fill_scale(float scale, FwdParams& p) {
+  if (scale == 0.f) {
+    p.scale_div = 24.0f;
+  } else {
+    if (!(scale > 0.f && scale <= 0.5f)) return false;
+    p.scale_div = (float)(1.0 / (double)scale);
+  }
+  p.scale_log2 = 1.4426950408889634f / p.scale_div;
+  return true;
+}
+
+// Final statistics of one (token, head) row from the running max m (raw,
+// unscaled scores) and the sum l: softmax_max = m / scale_div, or -inf for a
+// row without a valid index (l == 0); the output row is 0 there.
+__device__ __forceinline__ float final_max(float m_raw, float l, float scale_div) {
+  return l > 0.f ? __fdiv_rn(m_raw, scale_div) : -INFINITY;
+}
 
 // Split bounds in whole tiles, uneven when the tile count does not divide
 // (the tile-count split of dsa/ragged.py:141-143, generalised to a ragged

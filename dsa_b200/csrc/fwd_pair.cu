@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       const uint32_t e = (uint32_t)(warp - kSoftWarp0) >> 2;
       const int row = quad * 32 + lane;
       const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
-      const float c = 1.4426950408889634f / 24.0f;  // log2(e) / 24
+      const float c = p.scale_log2;  // log2(e) / scale_div
       float* const xch = reinterpret_cast<float*>(sbase + kOffX);  // [parity][quad][warp][3][lane]
       float* const mpub = reinterpret_cast<float*>(sbase + kOffM);  // [tile parity][quad][lane]
       const uint32_t r_slot0 = mapa_shared(base + kOffSlot, 1);
@@ -529,13 +529,12 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         if (e != 0) continue;
         const float f = (m_true == kNegFltMax) ? 1.f : ex2((m_w - m_true) * c);
         const size_t orow = (size_t)w.token * kPrHeads + row;
-        const float mout = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, 24.0f);
         if (p.split == 1) {
-          p.out_max[orow] = mout;
+          p.out_max[orow] = final_max(m_true, l, p.scale_div);
           p.out_sum[orow] = l * f;
         } else {
           const size_t pr = ((size_t)w.token * p.split + w.sp) * kPrHeads + row;
-          p.part_max[pr] = mout;
+          p.part_max[pr] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, p.scale_div);
           p.part_sum[pr] = l * f;
         }
         const uint32_t fb = it & 1u;
@@ -695,6 +694,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         tc_fence_after();
         const size_t orow = (size_t)w.token * kPrHeads + row;
         if (p.split == 1) {
+          const float ld = lf.x > 0.f ? lf.x : INFINITY;  // a row without a valid index is written as 0
           __nv_bfloat16* dst = p.out + orow * kDimLatent;
 #pragma unroll 1
           for (int cb = 0; cb < 512; cb += 32) {
@@ -704,7 +704,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             uint32_t h[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k)
-              h[k] = pack_bf16x2(__fdiv_rn(u2f(o[2 * k]), lf.x), __fdiv_rn(u2f(o[2 * k + 1]), lf.x));
+              h[k] = pack_bf16x2(__fdiv_rn(u2f(o[2 * k]), ld), __fdiv_rn(u2f(o[2 * k + 1]), ld));
             uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
 #pragma unroll
             for (int k = 0; k < 4; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);

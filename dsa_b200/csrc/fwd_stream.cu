@@ -275,8 +275,9 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
 
       // ---- online softmax: 8 threads per head row ----
       {
-        // raw (unscaled) scores; exp(s / 24 - m) = 2^(s * c - m * c) with c = log2(e) / 24
-        constexpr float c = 1.4426950408889634f / 24.0f;
+        // raw (unscaled) scores; exp(s / d - m) = 2^(s * c - m * c) with
+        // c = log2(e) / d, d = scale_div (24 for the reference's scale)
+        const float c = p.scale_log2;
         constexpr int kCols = kStBN / 8;
         const int r = ctid >> 3;
         const int c0 = (ctid & 7) * kCols;
@@ -361,16 +362,18 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
     // ---- epilogue (sm.m / sm.l final after the last softmax barrier) ----
     const float l0 = sm.l[g], l1 = sm.l[g + 8];
     if (p.split == 1) {
+      // a row without a valid index (l == 0, O == 0) is written as 0 (O / inf)
+      const float d0 = l0 > 0.f ? l0 : INFINITY, d1 = l1 > 0.f ? l1 : INFINITY;
       __nv_bfloat16* o0 = p.out + ((size_t)w.token * p.heads + h0 + g) * kDimLatent + cw * 128 + tq * 2;
       __nv_bfloat16* o1 = o0 + 8 * kDimLatent;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        *reinterpret_cast<uint32_t*>(o0 + j * 8) = pack_bf16x2(__fdiv_rn(acc[j][0], l0), __fdiv_rn(acc[j][1], l0));
-        *reinterpret_cast<uint32_t*>(o1 + j * 8) = pack_bf16x2(__fdiv_rn(acc[j][2], l1), __fdiv_rn(acc[j][3], l1));
+        *reinterpret_cast<uint32_t*>(o0 + j * 8) = pack_bf16x2(__fdiv_rn(acc[j][0], d0), __fdiv_rn(acc[j][1], d0));
+        *reinterpret_cast<uint32_t*>(o1 + j * 8) = pack_bf16x2(__fdiv_rn(acc[j][2], d1), __fdiv_rn(acc[j][3], d1));
       }
       if (ctid < kStHeads) {
         const float mr = sm.m[ctid];
-        p.out_max[(size_t)w.token * p.heads + h0 + ctid] = mr == kNegFltMax ? mr : __fdiv_rn(mr, 24.0f);
+        p.out_max[(size_t)w.token * p.heads + h0 + ctid] = final_max(mr, sm.l[ctid], p.scale_div);
         p.out_sum[(size_t)w.token * p.heads + h0 + ctid] = sm.l[ctid];
       }
     } else {
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
       }
       if (ctid < kStHeads) {
         const float mr = sm.m[ctid];
-        p.part_max[prow + ctid] = mr == kNegFltMax ? mr : __fdiv_rn(mr, 24.0f);
+        p.part_max[prow + ctid] = mr == kNegFltMax ? mr : __fdiv_rn(mr, p.scale_div);
         p.part_sum[prow + ctid] = sm.l[ctid];
       }
     }

@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const int quad = warp & 3;  // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;
     const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
-    const float c = 1.4426950408889634f / 24.0f;  // log2(e) / 24
+    const float c = p.scale_log2;  // log2(e) / scale_div
     uint8_t* const prow0 = sbase + kOffP + (uint32_t)(row >> 3) * 512u + (uint32_t)(row & 7) * 64u;
     const uint32_t* const mask_all = reinterpret_cast<const uint32_t*>(sbase + kOffMask);
     uint32_t g = 0, it = 0;
@@ -474,6 +474,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       const size_t orow = (size_t)w.token * kUmHeads + row;
       const int col0 = w.half * 256;
       if (p.split == 1) {
+        const float ld = l > 0.f ? l : INFINITY;  // a row without a valid index is written as 0
         __nv_bfloat16* dst = p.out + orow * kDimLatent + col0;
 #pragma unroll 1
         for (int cb = 0; cb < 256; cb += 32) {
@@ -483,13 +484,13 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
           uint32_t h[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k)
-            h[k] = pack_bf16x2(__fdiv_rn(u2f(o[2 * k]), l), __fdiv_rn(u2f(o[2 * k + 1]), l));
+            h[k] = pack_bf16x2(__fdiv_rn(u2f(o[2 * k]), ld), __fdiv_rn(u2f(o[2 * k + 1]), ld));
           uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
 #pragma unroll
           for (int k = 0; k < 4; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
         }
         if (w.half == 0) {
-          p.out_max[orow] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, 24.0f);
+          p.out_max[orow] = final_max(m_true, l, p.scale_div);
           p.out_sum[orow] = l * f;
         }
       } else {
@@ -507,7 +508,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
                                 u2f(o[4 * k + 3]) * f);
         }
         if (w.half == 0) {
-          p.part_max[prow_idx] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, 24.0f);
+          p.part_max[prow_idx] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, p.scale_div);
           p.part_sum[prow_idx] = l * f;
         }
       }

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kWmThreads, 2) fwd_warp_mma_kernel(FwdParams p
   if (ntiles > 0) issue_tile(0, 0);
   cp_async_commit();
 
-  const float inv_scale_div = 24.0f;
+  const float inv_scale_div = p.scale_div;  // scores / scale_div (24 for the reference's scale)
   for (int t = 0; t < ntiles; ++t) {
     const int stage = t & 1;
     if (t + 1 < ntiles) issue_tile(t + 1, stage ^ 1);
@@ -230,17 +230,19 @@ __global__ void __launch_bounds__(kWmThreads, 2) fwd_warp_mma_kernel(FwdParams p
   // ---- epilogue --------------------------------------------------------------
   const float l0 = sm.l[g], l1 = sm.l[g + 8];
   if (p.split == 1) {
+    // a row without a valid index (l == 0, O == 0) is written as 0 (O / inf)
+    const float d0 = l0 > 0.f ? l0 : INFINITY, d1 = l1 > 0.f ? l1 : INFINITY;
     __nv_bfloat16* o0 = p.out + ((size_t)token * p.heads + h0 + g) * kDimLatent + warp * 128 + tq * 2;
     __nv_bfloat16* o1 = o0 + 8 * kDimLatent;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       *reinterpret_cast<uint32_t*>(o0 + j * 8) =
-          pack_bf16x2(__fdiv_rn(acc[j][0], l0), __fdiv_rn(acc[j][1], l0));
+          pack_bf16x2(__fdiv_rn(acc[j][0], d0), __fdiv_rn(acc[j][1], d0));
       *reinterpret_cast<uint32_t*>(o1 + j * 8) =
-          pack_bf16x2(__fdiv_rn(acc[j][2], l1), __fdiv_rn(acc[j][3], l1));
+          pack_bf16x2(__fdiv_rn(acc[j][2], d1), __fdiv_rn(acc[j][3], d1));
     }
     if (tid < kWmHeads) {
-      p.out_max[(size_t)token * p.heads + h0 + tid] = sm.m[tid];
+      p.out_max[(size_t)token * p.heads + h0 + tid] = sm.l[tid] > 0.f ? sm.m[tid] : -INFINITY;
       p.out_sum[(size_t)token * p.heads + h0 + tid] = sm.l[tid];
     }
   } else {

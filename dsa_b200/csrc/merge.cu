@@ -1,7 +1,9 @@
 // FP32 split-KV merge (reference: merge_partials, dsa/merge.py:13-91).
 //
 // For one (token, head): m = max_s m_s, w_s = exp(m_s - m),
-// l = sum_s w_s l_s, o = sum_s w_s u_s / l -> BF16, stats (m, l).
+// l = sum_s w_s l_s, o = sum_s w_s u_s / l -> BF16, stats (m, l). A row
+// whose splits are all masked (every partial max -FLT_MAX, l == 0) gets
+// output 0, max -inf, sum 0.
 // Many splits: one block per (token, head): kMergeGroups groups of 128 threads, each
 // thread owning 4 consecutive latent columns, so every partial row is read
 // once with 16-byte loads. The split statistics are reduced across lanes;
@@ -84,12 +86,13 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(
     u.z += o.z;
     u.w += o.w;
   }
+  const float ld = l > 0.f ? l : INFINITY;  // no valid index in any split: output 0
   uint2 packed;
-  packed.x = pack_bf16x2(__fdiv_rn(u.x, l), __fdiv_rn(u.y, l));
-  packed.y = pack_bf16x2(__fdiv_rn(u.z, l), __fdiv_rn(u.w, l));
+  packed.x = pack_bf16x2(__fdiv_rn(u.x, ld), __fdiv_rn(u.y, ld));
+  packed.y = pack_bf16x2(__fdiv_rn(u.z, ld), __fdiv_rn(u.w, ld));
   *reinterpret_cast<uint2*>(out + (size_t)th * kDimLatent + c) = packed;
   if (threadIdx.x == 0) {
-    omax[th] = m;
+    omax[th] = l > 0.f ? m : -INFINITY;
     osum[th] = l;
   }
 }
@@ -144,16 +147,17 @@ __global__ void __launch_bounds__(32 * kWarpMergeWarps) merge_warp_kernel(
       }
     }
   }
+  const float ld = l > 0.f ? l : INFINITY;  // no valid index in any split: output 0
   uint2* dst = reinterpret_cast<uint2*>(out + (size_t)th * kDimLatent) + lane;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint2 packed;
-    packed.x = pack_bf16x2(__fdiv_rn(u[j].x, l), __fdiv_rn(u[j].y, l));
-    packed.y = pack_bf16x2(__fdiv_rn(u[j].z, l), __fdiv_rn(u[j].w, l));
+    packed.x = pack_bf16x2(__fdiv_rn(u[j].x, ld), __fdiv_rn(u[j].y, ld));
+    packed.y = pack_bf16x2(__fdiv_rn(u[j].z, ld), __fdiv_rn(u[j].w, ld));
     dst[32 * j] = packed;
   }
   if (lane == 0) {
-    omax[th] = m;
+    omax[th] = l > 0.f ? m : -INFINITY;
     osum[th] = l;
   }
 }

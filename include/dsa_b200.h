@@ -17,8 +17,13 @@
  *                                    masked (their address is clamped), and
  *                                    duplicates keep their repeated weight
  *   output       BF16 [B, SQ, H, 512]
- *   softmax_max  FP32 [B, 1, SQ, H]  max_j s_j, with s_j = (q.kv_j + qr.kr_j)/24
+ *   softmax_max  FP32 [B, 1, SQ, H]  max_j s_j, with s_j = (q.kv_j + qr.kr_j) * scale
+ *                                    (scale 1/sqrt(576) = 1/24 unless the caller sets one)
  *   softmax_sum  FP32 [B, 1, SQ, H]  sum_j exp(s_j - max)
+ *
+ * A (token, head) row whose indices are all outside [0, L) gets output 0,
+ * softmax_max -inf and softmax_sum 0 (the reference requires at least one
+ * valid index per query and leaves this case undefined, dsa/api.py:82-91).
  *
  * Every pointer is a device pointer on the current device. No function
  * allocates device memory: temporaries (split-KV partials) live in a
@@ -39,7 +44,7 @@
 extern "C" {
 #endif
 
-#define DSA_B200_ABI_VERSION 1
+#define DSA_B200_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define DSA_B200_API __attribute__((visibility("default")))
@@ -100,6 +105,9 @@ typedef struct dsa_fwd_args {
   uint64_t workspace_bytes;
   int32_t* status;          /* optional device word; kernels only OR error bits
                                into it (never clear it). NULL disables reporting. */
+  float scale;              /* softmax scale on q.kv + qr.kr, in (0, 0.5]; 0 selects the
+                               reference's fixed 1/24 (README.md:81-84). The scale_value
+                               of the vendor operator's interface. */
 } dsa_fwd_args_t;
 
 /* ABI version (DSA_B200_ABI_VERSION of the built library). No reference

@@ -122,7 +122,8 @@ def make_indices_variant(batch, queries, length, selected, seed: int, variant: s
 
 
 def reference_forward(q, kv, q_rope, k_rope, indices, chunk: int = 16,
-                      query_range: Tuple[int, int] | None = None):
+                      query_range: Tuple[int, int] | None = None,
+                      scale: float | None = None, defined_invalid: bool = False):
     """FP32 oracle of tools/review.py:123-145, on the CPU.
 
     Returns ``(output, softmax_max, softmax_sum)`` as FP32 tensors shaped
@@ -130,6 +131,13 @@ def reference_forward(q, kv, q_rope, k_rope, indices, chunk: int = 16,
     the computation to flattened query rows ``[lo, hi)`` of ``B*SQ`` (the
     result then holds only those rows, shaped ``[hi-lo, H, 512]`` and
     ``[hi-lo, H]``) so that large configs can be checked on a sample.
+
+    ``scale=None`` divides the scores by 24 exactly as the reference does
+    (tools/review.py:139); a given scale multiplies them (the vendor
+    operator's ``scale_value``). The reference leaves a query without any
+    valid index undefined (its math yields NaN); ``defined_invalid=True``
+    returns the behaviour this build defines for it instead: output 0,
+    softmax_max -inf, softmax_sum 0.
     """
     prev = torch.get_float32_matmul_precision()
     torch.set_float32_matmul_precision("highest")
@@ -162,12 +170,19 @@ def reference_forward(q, kv, q_rope, k_rope, indices, chunk: int = 16,
             selected = kv[bi, index, 0].float()
             rope = k_rope[bi, index, 0].float()
             score = (torch.bmm(q[bi, start:end].float(), selected.transpose(1, 2))
-                     + torch.bmm(q_rope[bi, start:end].float(), rope.transpose(1, 2))) / SCALE_DIVISOR
+                     + torch.bmm(q_rope[bi, start:end].float(), rope.transpose(1, 2)))
+            score = score / SCALE_DIVISOR if scale is None else score * scale
             score.masked_fill_(~valid[:, None, :], -float("inf"))
             maximum = score.amax(-1)
             exponent = (score - maximum[..., None]).exp()
             denominator = exponent.sum(-1)
             o = torch.bmm(exponent / denominator[..., None], selected)
+            if defined_invalid:
+                empty = ~valid.any(-1)  # [n]: no valid index in this query's row
+                if bool(empty.any()):
+                    o[empty] = 0.0
+                    maximum[empty] = -float("inf")
+                    denominator[empty] = 0.0
             if query_range is None:
                 out[bi, start:end] = o
                 mx[bi, 0, start:end] = maximum
