@@ -39,11 +39,16 @@
 //              the P transfer of consecutive tiles overlap. Key validity comes
 //              from the indices (loaded a tile ahead), so a stage is free as
 //              soon as its QK MMAs complete. 16-19 QK issuers (tile g ->
-//              issuer g % 4 and S buffer g % 4: issuing a tcgen05.mma occupies
-//              the issuing warp's scheduler, so the 36 MMAs of each tile are
-//              spread over the four schedulers).
+//              issuer g % 4: issuing a tcgen05.mma occupies the issuing warp's
+//              scheduler, so the 36 MMAs of each tile are spread over the four
+//              schedulers) into S buffer g % 4 (a buffer returns to the
+//              issuers only after its softmax read). At an
+//              item boundary the issuers also load three of the nine Q chunks
+//              of their lane quadrant, and the next item's Q is prefetched
+//              into L2 eight tiles ahead.
 //   value CTA: 0-4 gather of the 512 latent dims (warp w owns stage w), 6 PV
-//              issuer, 8-11 rescale and epilogue (O / l -> output).
+//              issuer, 8-19 rescale and epilogue (three warps per lane
+//              quadrant, O * (1/l) -> output with 32-byte stores).
 // Every wait is bounded and reports through the status word; no TMA and no
 // multicast loads are used.
 #include "umma_ptx.cuh"
@@ -58,10 +63,14 @@ constexpr int kPrHeads = 128;
 constexpr int kKStages = 6;     // score CTA: gathered full rows
 constexpr int kSlots = 5;       // value CTA: gathered value rows and P slots
 constexpr int kSBufs = 4;       // score CTA: S accumulators in TMEM
+constexpr int kQkIssuers = 4;   // score CTA: QK issuer warps, one per scheduler
 constexpr int kPrThreads = 640;
 constexpr int kPvWarp = 6;      // value CTA
-constexpr int kSoftWarp0 = 8;   // score CTA softmax (8 warps) / value CTA rescale+epilogue (4 warps)
+constexpr int kSoftWarp0 = 8;   // score CTA softmax (8 warps) / value CTA rescale+epilogue (12 warps)
 constexpr int kSoftWarps = 8;
+constexpr int kEpiWarps = 12;   // value CTA: warps 8..19, three per TMEM lane quadrant
+// first 32-column chunk of O owned by epilogue part 0, 1, 2 (chunks 0-5, 6-10, 11-15)
+__host__ __device__ constexpr int epi_chunk0(int part) { return part == 0 ? 0 : 5 * part + 1; }
 constexpr int kQkWarp0 = 16;    // score CTA: QK issuer i = warp 16 + i (one per scheduler), S buffer i
 constexpr int kQkSteps = kDimQK / 16;  // 36
 
@@ -95,8 +104,8 @@ enum Bar {
   kVFull0 = kSlotFree0 + kSlots,
   kPFull0 = kVFull0 + kSlots,       // P message landed (complete_tx)
   kReq = kPFull0 + kSlots,          // a rescale or epilogue request is posted
-  kReqDone,                         // rescale done (4 warps)
-  kOFree,                           // epilogue has read O (4 warps)
+  kReqDone,                         // rescale done (kEpiWarps warps)
+  kOFree,                           // epilogue has read O (kEpiWarps warps)
   kFin0,                            // 2: (l, f) of an item landed (complete_tx)
   kBarCount = kFin0 + 2
 };
@@ -241,6 +250,47 @@ __device__ __forceinline__ void gather_rows(uint32_t stage, const __nv_bfloat16*
   }
 }
 
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* h) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+               "r"(h[3]), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7])
+               : "memory");
+}
+
+// 32 FP32 values (O columns of one head row) * rl -> 32 BF16 at dst (64 B).
+// Each thread writes its own row, so a warp store touches 32 rows: 32-byte
+// stores (whole L2 sectors, half the requests of 16-byte ones) when dst is
+// 32-byte aligned (`wide`), 16-byte stores otherwise.
+__device__ __forceinline__ void store_bf16_row32(__nv_bfloat16* dst, const uint32_t* o, float rl, bool wide) {
+  uint32_t h[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) h[k] = pack_bf16x2(__uint_as_float(o[2 * k]) * rl, __uint_as_float(o[2 * k + 1]) * rl);
+  if (wide) {
+    st_global_v8(dst, h);
+    st_global_v8(dst + 16, h + 8);
+  } else {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+  }
+}
+
+// Chunk `ch` (dims 64ch..64ch+63; ch == 8: the 64 rope dims) of one Q head
+// row -> 32 TMEM columns of this thread's lane (BF16 pairs).
+__device__ __forceinline__ void load_q_chunk(const FwdParams& p, size_t qrow, int ch, uint32_t taddr) {
+  const uint4* s4 = ch < 8 ? reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent) + ch * 8
+                           : reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
+  uint32_t r[32];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint4 v = __ldg(s4 + k);
+    r[4 * k] = v.x;
+    r[4 * k + 1] = v.y;
+    r[4 * k + 2] = v.z;
+    r[4 * k + 3] = v.w;
+  }
+  tmem_st32(taddr, r);
+}
+
 __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -262,14 +312,14 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         mbar_init(bar(kFull0 + s), 1);
         mbar_init(bar(kEmpty0 + s), 1);
       }
-      mbar_init(bar(kQFull), kSoftWarps);
-      mbar_init(bar(kQSeen), kSBufs);
+      mbar_init(bar(kQFull), kSoftWarps + kQkIssuers);  // Q chunks: 8 softmax warps + 4 QK issuers
+      mbar_init(bar(kQSeen), kQkIssuers);
       for (int i = 0; i < kSBufs; ++i) {
         mbar_init(bar(kSFull0 + i), 1);
         mbar_init(bar(kSFree0 + i), 4);
       }
-      mbar_init(bar(kFinFree0), 4);
-      mbar_init(bar(kFinFree0 + 1), 4);
+      mbar_init(bar(kFinFree0), kEpiWarps);
+      mbar_init(bar(kFinFree0 + 1), kEpiWarps);
       for (int q = 0; q < 4; ++q) {
         mbar_init(bar(kXchg0 + q), 2);
         mbar_init(bar(kMReady0 + q), 1);
@@ -280,8 +330,8 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         mbar_init(bar(kPFull0 + s), 1);
       }
       mbar_init(bar(kReq), 1);
-      mbar_init(bar(kReqDone), 4);
-      mbar_init(bar(kOFree), 4);
+      mbar_init(bar(kReqDone), kEpiWarps);
+      mbar_init(bar(kOFree), kEpiWarps);
       mbar_init(bar(kFin0), 1);
       mbar_init(bar(kFin0 + 1), 1);
     }
@@ -340,23 +390,38 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         idx_nx = idx_nx2;
       }
     } else if (warp >= kQkWarp0) {
-      // ---- QK issuer i: S buffer i <- Q (TMEM) . K^T (stage g % 6) for tiles g = i mod 4 ----
+      // ---- QK issuer i: S buffer g % 4 <- Q (TMEM) . K^T (stage g % 6) for tiles g = i mod 4 ----
       const uint32_t i = (uint32_t)(warp - kQkWarp0);
       const uint32_t idesc_qk = idesc_bf16(128, kPrBN, false, false);
-      const uint32_t d = tmem + kTmemS + i * kPrBN;
-      uint32_t g = 0, it = 0, n = 0;  // n: tiles this issuer ran
+      uint32_t g = 0, it = 0;
+      const uint32_t t_lane = (uint32_t)(i * 32) << 16;  // warp 16 + i accesses lane quadrant i
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
+        // Q chunks 2, 5, 8 of quadrant i's head rows. Both softmax warps of
+        // the quadrant finished the previous item (its item-end exchange),
+        // so every QK MMA of that item has completed.
+        if (it > 0 && !(ok = wait_warp(bar(kXchg0 + i), (it - 1) & 1u, abort_flag))) break;
+        {
+          const size_t qrow = (size_t)w.token * kPrHeads + i * 32 + lane;
+#pragma unroll 1
+          for (int ch = 2; ch < 9; ch += 3) load_q_chunk(p, qrow, ch, tmem + t_lane + kTmemQ + ch * 32);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kQFull));
+        }
         // Every issuer observes every item's Q and acknowledges it, so none
         // can fall a barrier phase behind.
         if (!(ok = wait_warp(bar(kQFull), it & 1u, abort_flag))) break;
         if (elect_one()) mbar_arrive(bar(kQSeen));
         __syncwarp();
         for (int t = 0; t < w.ntiles; ++t, ++g) {
-          if (g % kSBufs != i) continue;
-          const uint32_t s = g % kKStages;
+          if (g % kQkIssuers != i) continue;
+          const uint32_t s = g % kKStages, b = g % kSBufs;
+          const uint32_t d = tmem + kTmemS + b * kPrBN;
           if (!(ok = wait_warp(bar(kFull0 + s), (g / kKStages) & 1u, abort_flag))) break;
-          if (n > 0 && !(ok = wait_warp(bar(kSFree0 + i), (n - 1) & 1u, abort_flag))) break;
+          // S buffer b was last used by tile g - kSBufs: its softmax has read it
+          if (g >= kSBufs && !(ok = wait_warp(bar(kSFree0 + b), ((g / kSBufs) - 1) & 1u, abort_flag))) break;
           tc_fence_after();
           const uint32_t stage = base + kOffK + s * kKStage;
           if (elect_one()) {
@@ -366,11 +431,10 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
                   smem_desc(stage + (ks >> 2) * kBlk + (uint32_t)(ks & 3) * 32u, 16, 1024, kLayoutSw128);
               mma_bf16_ts(d, tmem + kTmemQ + (uint32_t)ks * 8u, bd, idesc_qk, ks > 0 ? 1u : 0u);
             }
-            mma_commit(bar(kSFull0 + i));
+            mma_commit(bar(kSFull0 + b));
             mma_commit(bar(kEmpty0 + s));
           }
           __syncwarp();
-          ++n;
         }
       }
     } else if (warp >= kSoftWarp0 && warp < kSoftWarp0 + kSoftWarps) {
@@ -396,28 +460,15 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       uint32_t g = 0, it = 0;
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
-        // Q of this head row -> TMEM columns [0, 288) (chunks ch with ch % 2 == e).
-        // The previous item's QK MMAs are complete (every S was waited for)
-        // and every issuer has seen the previous item's Q.
+        // Q of this head row -> TMEM columns [0, 288): chunks e, e + 3, e + 6
+        // here, chunks 2, 5, 8 by the quadrant's QK issuer. The previous
+        // item's QK MMAs are complete (every S was waited for) and every
+        // issuer has seen the previous item's Q.
         if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag))) break;
         {
           const size_t qrow = (size_t)w.token * kPrHeads + row;
-          const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
-          const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
 #pragma unroll 1
-          for (int ch = (int)e; ch < 9; ch += 2) {
-            const uint4* s4 = ch < 8 ? src + ch * 8 : rsrc;
-            uint32_t r[32];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint4 v = __ldg(s4 + k);
-              r[4 * k] = v.x;
-              r[4 * k + 1] = v.y;
-              r[4 * k + 2] = v.z;
-              r[4 * k + 3] = v.w;
-            }
-            tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
-          }
+          for (int ch = (int)e; ch < 9; ch += 3) load_q_chunk(p, qrow, ch, tmem + t_lane + kTmemQ + ch * 32);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
@@ -429,6 +480,15 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         float l = 0.f;              // sum over this warp's tiles, relative to m_w
         for (int t = 0; t < w.ntiles; ++t, ++g) {
           if ((g & 1u) != e) continue;
+          if (t == max(w.ntiles - 8, 0) && quad == 0 && item + ncl < n_items && lane < 9) {
+            // the next item's Q rows -> L2 (128 KB latent + 16 KB rope), so
+            // that its load at the item boundary hits L2
+            const size_t qn = (size_t)((item + ncl) / p.split) * kPrHeads;
+            if (lane < 8)
+              prefetch_l2_bulk(p.q + qn * kDimLatent + (size_t)lane * 8192, 16384u);
+            else
+              prefetch_l2_bulk(p.q_rope + qn * kDimRope, 16384u);
+          }
           const uint32_t i = g % kSBufs, ps = g % kSlots;
           const int idx = idx_nxt;  // this tile's indices (loaded one tile ahead)
           pcursor_advance(p, n_items, ncl, nxt, 2);
@@ -636,9 +696,12 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         }
         __syncwarp();
       }
-    } else if (warp >= kSoftWarp0 && warp < kSoftWarp0 + 4) {
-      // ---- rescale requests and epilogue (one head row per thread) ----
+    } else if (warp >= kSoftWarp0 && warp < kSoftWarp0 + kEpiWarps) {
+      // ---- rescale requests and epilogue: one head row per thread, warp part
+      // `part` of its lane quadrant owns O columns [cb0, cb1) ----
       const int quad = warp & 3;
+      const int part = (warp - kSoftWarp0) >> 2;
+      const int cb0 = 32 * epi_chunk0(part), cb1 = 32 * epi_chunk0(part + 1);
       const int row = quad * 32 + lane;
       const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
       const volatile uint32_t* const req = reinterpret_cast<const volatile uint32_t*>(sbase + kOffReq);
@@ -664,7 +727,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             tc_fence_after();
             uint32_t o[32];
 #pragma unroll 1
-            for (int cb = 0; cb < 512; cb += 32) {
+            for (int cb = cb0; cb < cb1; cb += 32) {
               const uint32_t a = tmem + t_lane + kTmemO + cb;
               tmem_ld32(a, o);
               tmem_wait_ld();
@@ -686,7 +749,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         const float2 lf = make_float2(lfp[0], lfp[1]);
         __syncwarp();
         if (lane == 0) {
-          if (quad == 0) mbar_arrive_expect_tx(bar(kFin0 + fb), kFinBytes);  // for item it + 2
+          if (quad == 0 && part == 0) mbar_arrive_expect_tx(bar(kFin0 + fb), kFinBytes);  // for item it + 2
           mbar_arrive_remote(r_finfree0 + 8u * fb);
         }
         const uint32_t gl = g_end - 1;
@@ -694,26 +757,30 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         tc_fence_after();
         const size_t orow = (size_t)w.token * kPrHeads + row;
         if (p.split == 1) {
-          const float ld = lf.x > 0.f ? lf.x : INFINITY;  // a row without a valid index is written as 0
+          // O * (1/l) with the correctly rounded reciprocal (within an FP32 ulp of
+          // O / l); a row without a valid index (l == 0) is written as 0
+          const float rl = lf.x > 0.f ? __frcp_rn(lf.x) : 0.f;
           __nv_bfloat16* dst = p.out + orow * kDimLatent;
+          const bool wide = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;  // rows are 1024 B apart
+          // two 32-column chunks in flight: the next load overlaps this store
+          uint32_t oa[32], ob[32];
+          tmem_ld32(tmem + t_lane + kTmemO + cb0, oa);
 #pragma unroll 1
-          for (int cb = 0; cb < 512; cb += 32) {
-            uint32_t o[32];
-            tmem_ld32(tmem + t_lane + kTmemO + cb, o);
-            tmem_wait_ld();
-            uint32_t h[16];
-#pragma unroll
-            for (int k = 0; k < 16; ++k)
-              h[k] = pack_bf16x2(__fdiv_rn(u2f(o[2 * k]), ld), __fdiv_rn(u2f(o[2 * k + 1]), ld));
-            uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+          for (int cb = cb0; cb < cb1; cb += 64) {
+            tmem_wait_ld_regs32(oa);
+            const bool more = cb + 32 < cb1;
+            if (more) tmem_ld32(tmem + t_lane + kTmemO + cb + 32, ob);
+            store_bf16_row32(dst + cb, oa, rl, wide);
+            if (!more) break;
+            tmem_wait_ld_regs32(ob);
+            if (cb + 64 < cb1) tmem_ld32(tmem + t_lane + kTmemO + cb + 64, oa);
+            store_bf16_row32(dst + cb + 32, ob, rl, wide);
           }
         } else {
           const size_t pr = ((size_t)w.token * p.split + w.sp) * kPrHeads + row;
           float* dst = p.part_num + pr * kDimLatent;
 #pragma unroll 1
-          for (int cb = 0; cb < 512; cb += 32) {
+          for (int cb = cb0; cb < cb1; cb += 32) {
             uint32_t o[32];
             tmem_ld32(tmem + t_lane + kTmemO + cb, o);
             tmem_wait_ld();

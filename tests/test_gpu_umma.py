@@ -29,8 +29,16 @@ def _run(data, split, pv_cols):
 
 
 def _check(got, ref):
-    metrics = oracle.accuracy([t.float().cpu() for t in got], ref)
-    assert oracle.passes(metrics), metrics
+    got = [t.float().cpu() for t in got]
+    metrics = oracle.accuracy(got, ref)
+    if not oracle.passes(metrics):
+        # locate the worst (token, head) of each statistic for the report
+        where = {}
+        for name, a, b in (("maximum", got[1], ref[1]), ("denominator", got[2], ref[2])):
+            d = ((a - b).abs() / b.abs().max()).reshape(-1)
+            k = int(d.argmax())
+            where[name] = (k, float(a.reshape(-1)[k]), float(b.reshape(-1)[k]), float(d[k]))
+        raise AssertionError(f"{metrics}\nworst (flat index, got, ref, err): {where}")
     return metrics
 
 
