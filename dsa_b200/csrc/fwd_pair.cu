@@ -60,18 +60,25 @@ using namespace umma;
 
 constexpr int kPrBN = 32;       // keys per tile
 constexpr int kPrHeads = 128;
-constexpr int kKStages = 6;     // score CTA: gathered full rows
-constexpr int kSlots = 5;       // value CTA: gathered value rows and P slots
-constexpr int kSBufs = 4;       // score CTA: S accumulators in TMEM
-constexpr int kQkIssuers = 4;   // score CTA: QK issuer warps, one per scheduler
+// Tile g of the cluster's sequence uses stage, S buffer and P slot g % 6,
+// gather warp and QK issuer g % 6 and softmax warp g % 2 of each lane
+// quadrant: every mbarrier is waited on by one role whose consecutive waits
+// on it are one phase apart, the condition for parity waits to be exact.
+constexpr int kKStages = 6;     // score CTA: gathered full rows (gather warp w owns stage w)
+constexpr int kSBufs = 6;       // score CTA: S accumulators in TMEM
+constexpr int kQkIssuers = 6;   // score CTA: QK issuer i takes tiles g = i mod 6
+constexpr int kQkQHelpers = 4;  // issuers 0-3 also load Q chunks of their lane quadrant
+constexpr int kVStages = 5;     // value CTA: gathered value rows
+constexpr int kPSlots = 6;      // value CTA: P slots
 constexpr int kPrThreads = 640;
-constexpr int kPvWarp = 6;      // value CTA
-constexpr int kSoftWarp0 = 8;   // score CTA softmax (8 warps) / value CTA rescale+epilogue (12 warps)
+constexpr int kPvWarp = 6;      // value CTA: gather 0-4, PV issuer 6, rescale+epilogue 8-19
+constexpr int kSoftWarp0 = 6;   // score CTA: gather 0-5, softmax 6-13, QK issuers 14-19
 constexpr int kSoftWarps = 8;
+constexpr int kEpiWarp0 = 8;
 constexpr int kEpiWarps = 12;   // value CTA: warps 8..19, three per TMEM lane quadrant
 // first 32-column chunk of O owned by epilogue part 0, 1, 2 (chunks 0-5, 6-10, 11-15)
 __host__ __device__ constexpr int epi_chunk0(int part) { return part == 0 ? 0 : 5 * part + 1; }
-constexpr int kQkWarp0 = 16;    // score CTA: QK issuer i = warp 16 + i (one per scheduler), S buffer i
+constexpr int kQkWarp0 = 14;    // score CTA: QK issuer i = warp 14 + i
 constexpr int kQkSteps = kDimQK / 16;  // 36
 
 // Shared memory (byte offsets from a 1024-aligned base; same layout in both
@@ -98,12 +105,12 @@ enum Bar {
   kFinFree0 = kSFree0 + kSBufs,     // 2: value CTA has read the (l, f) buffer
   kXchg0 = kFinFree0 + 2,           // 4: per lane quadrant, both softmax warps posted their item totals
   kMReady0 = kXchg0 + 4,            // 4: per lane quadrant, the running max of the latest tile is posted
-  // both CTAs: PV of slot s's tile done (score CTA: P slot free, value CTA: value stage free)
-  kSlotFree0 = kMReady0 + 4,
+  kPSlotFree0 = kMReady0 + 4,       // P slot's PV done (commit multicast from the value CTA)
   // value CTA
-  kVFull0 = kSlotFree0 + kSlots,
-  kPFull0 = kVFull0 + kSlots,       // P message landed (complete_tx)
-  kReq = kPFull0 + kSlots,          // a rescale or epilogue request is posted
+  kVFull0 = kPSlotFree0 + kPSlots,
+  kVFree0 = kVFull0 + kVStages,     // value stage's PV done
+  kPFull0 = kVFree0 + kVStages,     // P message landed (complete_tx)
+  kReq = kPFull0 + kPSlots,         // a rescale or epilogue request is posted
   kReqDone,                         // rescale done (kEpiWarps warps)
   kOFree,                           // epilogue has read O (kEpiWarps warps)
   kFin0,                            // 2: (l, f) of an item landed (complete_tx)
@@ -117,8 +124,8 @@ constexpr uint32_t kOffMask = kOffReq + 8u;             // score CTA: one word p
 constexpr uint32_t kOffData = 1024u;
 constexpr uint32_t kOffK = kOffData;                     // score CTA stages
 constexpr uint32_t kOffV = kOffData;                     // value CTA stages
-constexpr uint32_t kOffSlot = kOffV + kSlots * kVStage;  // value CTA P slots
-constexpr uint32_t kOffFin = kOffSlot + kSlots * kSlotBytes;
+constexpr uint32_t kOffSlot = kOffV + kVStages * kVStage;  // value CTA P slots
+constexpr uint32_t kOffFin = kOffSlot + kPSlots * kSlotBytes;
 constexpr uint32_t kOffX = kOffK + kKStages * kKStage;   // score CTA: [2][4 quads][2 warps][3][32] floats
 constexpr uint32_t kOffM = kOffX + 2u * 4u * 2u * 3u * 32u * 4u;  // score CTA: [2][4 quads][32] running maxima
 constexpr uint32_t kSmemScore = kOffM + 2u * 4u * 32u * 4u;
@@ -312,7 +319,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         mbar_init(bar(kFull0 + s), 1);
         mbar_init(bar(kEmpty0 + s), 1);
       }
-      mbar_init(bar(kQFull), kSoftWarps + kQkIssuers);  // Q chunks: 8 softmax warps + 4 QK issuers
+      mbar_init(bar(kQFull), kSoftWarps + kQkQHelpers);  // Q chunks: 8 softmax warps + 4 QK issuers
       mbar_init(bar(kQSeen), kQkIssuers);
       for (int i = 0; i < kSBufs; ++i) {
         mbar_init(bar(kSFull0 + i), 1);
@@ -324,18 +331,19 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         mbar_init(bar(kXchg0 + q), 2);
         mbar_init(bar(kMReady0 + q), 1);
       }
+      for (int s = 0; s < kPSlots; ++s) mbar_init(bar(kPSlotFree0 + s), 1);
     } else {
-      for (int s = 0; s < kSlots; ++s) {
+      for (int s = 0; s < kVStages; ++s) {
         mbar_init(bar(kVFull0 + s), 1);
-        mbar_init(bar(kPFull0 + s), 1);
+        mbar_init(bar(kVFree0 + s), 1);
       }
+      for (int s = 0; s < kPSlots; ++s) mbar_init(bar(kPFull0 + s), 1);
       mbar_init(bar(kReq), 1);
       mbar_init(bar(kReqDone), kEpiWarps);
       mbar_init(bar(kOFree), kEpiWarps);
       mbar_init(bar(kFin0), 1);
       mbar_init(bar(kFin0 + 1), 1);
     }
-    for (int s = 0; s < kSlots; ++s) mbar_init(bar(kSlotFree0 + s), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -350,7 +358,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
   // The value CTA arms its P slots and (l, f) buffers before the score CTA
   // can send anything (the cluster barrier below orders the two).
   if (rank == 1 && threadIdx.x == 0) {
-    for (int s = 0; s < kSlots; ++s) mbar_arrive_expect_tx(bar(kPFull0 + s), kMsgBytes);
+    for (int s = 0; s < kPSlots; ++s) mbar_arrive_expect_tx(bar(kPFull0 + s), kMsgBytes);
     mbar_arrive_expect_tx(bar(kFin0), kFinBytes);
     mbar_arrive_expect_tx(bar(kFin0 + 1), kFinBytes);
   }
@@ -389,20 +397,21 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         idx_cur = idx_nx;
         idx_nx = idx_nx2;
       }
-    } else if (warp >= kQkWarp0) {
-      // ---- QK issuer i: S buffer g % 4 <- Q (TMEM) . K^T (stage g % 6) for tiles g = i mod 4 ----
+    } else if (warp >= kQkWarp0 && warp < kQkWarp0 + kQkIssuers) {
+      // ---- QK issuer i: S buffer g % 6 <- Q (TMEM) . K^T (stage g % 6) for tiles g = i mod 6 ----
       const uint32_t i = (uint32_t)(warp - kQkWarp0);
       const uint32_t idesc_qk = idesc_bf16(128, kPrBN, false, false);
       uint32_t g = 0, it = 0;
-      const uint32_t t_lane = (uint32_t)(i * 32) << 16;  // warp 16 + i accesses lane quadrant i
+      const int quad = warp & 3;  // TMEM lane quadrant this warp can access
+      const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
-        // Q chunks 2, 5, 8 of quadrant i's head rows. Both softmax warps of
-        // the quadrant finished the previous item (its item-end exchange),
-        // so every QK MMA of that item has completed.
-        if (it > 0 && !(ok = wait_warp(bar(kXchg0 + i), (it - 1) & 1u, abort_flag))) break;
-        {
-          const size_t qrow = (size_t)w.token * kPrHeads + i * 32 + lane;
+        // Issuers 0-3: Q chunks 2, 5, 8 of their lane quadrant's head rows.
+        // Both softmax warps of the quadrant finished the previous item (its
+        // item-end exchange), so every QK MMA of that item has completed.
+        if (i < (uint32_t)kQkQHelpers) {
+          if (it > 0 && !(ok = wait_warp(bar(kXchg0 + quad), (it - 1) & 1u, abort_flag))) break;
+          const size_t qrow = (size_t)w.token * kPrHeads + quad * 32 + lane;
 #pragma unroll 1
           for (int ch = 2; ch < 9; ch += 3) load_q_chunk(p, qrow, ch, tmem + t_lane + kTmemQ + ch * 32);
           tmem_wait_st();
@@ -420,7 +429,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           const uint32_t s = g % kKStages, b = g % kSBufs;
           const uint32_t d = tmem + kTmemS + b * kPrBN;
           if (!(ok = wait_warp(bar(kFull0 + s), (g / kKStages) & 1u, abort_flag))) break;
-          // S buffer b was last used by tile g - kSBufs: its softmax has read it
+          // S buffer b was last used by tile g - 6 (this issuer's): its softmax has read it
           if (g >= kSBufs && !(ok = wait_warp(bar(kSFree0 + b), ((g / kSBufs) - 1) & 1u, abort_flag))) break;
           tc_fence_after();
           const uint32_t stage = base + kOffK + s * kKStage;
@@ -489,7 +498,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             else
               prefetch_l2_bulk(p.q_rope + qn * kDimRope, 16384u);
           }
-          const uint32_t i = g % kSBufs, ps = g % kSlots;
+          const uint32_t i = g % kSBufs, ps = g % kPSlots;
           const int idx = idx_nxt;  // this tile's indices (loaded one tile ahead)
           pcursor_advance(p, n_items, ncl, nxt, 2);
           idx_nxt = pcursor_index(p, nxt, n_items, lane);
@@ -555,8 +564,8 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           }
           l += psum[0];
           const uint32_t flag = __any_sync(0xffffffffu, resc) ? 1u : 0u;
-          // P slot ps is free once the PV of tile g - 5 is done
-          if (g >= kSlots && !(ok = wait_warp(bar(kSlotFree0 + ps), ((g / kSlots) - 1) & 1u, abort_flag)))
+          // P slot ps is free once the PV of tile g - 6 (this warp's) is done
+          if (g >= kPSlots && !(ok = wait_warp(bar(kPSlotFree0 + ps), ((g / kPSlots) - 1) & 1u, abort_flag)))
             break;
           const uint32_t slot = r_slot0 + ps * kSlotBytes;
           const uint32_t pbar = r_pfull0 + 8u * ps;
@@ -601,13 +610,15 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         if (it >= 2 && !(ok = wait_warp(bar(kFinFree0 + fb), ((it >> 1) - 1) & 1u, abort_flag, true))) break;
         st_async_b32x2(r_fin0 + fb * kFinBytes + (uint32_t)row * 8u, r_finbar0 + 8u * fb, f2u(l), f2u(f));
       }
-      // Drain: the value CTA's last slot credits and (l, f) acknowledgements
-      // arrive here; wait for them before the CTA can exit.
+      // Drain: the value CTA's last P-slot credits and (l, f) acknowledgements
+      // arrive here; wait for them before the CTA can exit. Each warp waits
+      // for the credits of its own tiles among the last kPSlots.
+      for (uint32_t k = 0; ok && k < (uint32_t)kPSlots && k < g; ++k) {
+        const uint32_t gl = g - 1 - k;
+        if ((gl & 1u) != e) continue;
+        ok = wait_warp(bar(kPSlotFree0 + gl % kPSlots), (gl / kPSlots) & 1u, abort_flag);
+      }
       if (ok && e == 0) {
-        for (uint32_t k = 0; k < (uint32_t)kSlots && k < g; ++k) {
-          const uint32_t gl = g - 1 - k;
-          if (!(ok = wait_warp(bar(kSlotFree0 + gl % kSlots), (gl / kSlots) & 1u, abort_flag))) break;
-        }
         for (uint32_t k = 0; ok && k < 2u && k < it; ++k) {
           const uint32_t il = it - 1 - k;
           ok = wait_warp(bar(kFinFree0 + (il & 1u)), (il >> 1) & 1u, abort_flag, true);
@@ -616,20 +627,20 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
     }
   } else {
     // =============================== value CTA ===============================
-    if (warp < kSlots) {
+    if (warp < kVStages) {
       // ---- gather of the 512 latent dims: warp w fills stage w for tiles g = w, w+5, ... ----
       const uint32_t s = (uint32_t)warp;
       const uint32_t stage = base + kOffV + s * kVStage;
       PCursor cur = pcursor_start(p, n_items, cid, ncl, (int)s);
       PCursor nx = cur;
-      pcursor_advance(p, n_items, ncl, nx, kSlots);
+      pcursor_advance(p, n_items, ncl, nx, kVStages);
       PCursor nx2 = nx;
-      pcursor_advance(p, n_items, ncl, nx2, kSlots);
+      pcursor_advance(p, n_items, ncl, nx2, kVStages);
       int idx_cur = pcursor_index(p, cur, n_items, lane);
       int idx_nx = pcursor_index(p, nx, n_items, lane);
       uint32_t n = 0;
       while (cur.item < n_items) {
-        if (n > 0 && !(ok = wait_warp(bar(kSlotFree0 + s), (n - 1) & 1u, abort_flag, true))) break;
+        if (n > 0 && !(ok = wait_warp(bar(kVFree0 + s), (n - 1) & 1u, abort_flag))) break;
         const int row = min(max(idx_cur, 0), L - 1);  // invalid rows get P = 0
         gather_rows(stage, p.kv + (size_t)cur.w.batch * L * kDimLatent, nullptr, row, lane, false);
         cp_async_commit();
@@ -641,7 +652,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         ++n;
         cur = nx;
         nx = nx2;
-        pcursor_advance(p, n_items, ncl, nx2, kSlots);
+        pcursor_advance(p, n_items, ncl, nx2, kVStages);
         idx_cur = idx_nx;
         idx_nx = idx_nx2;
       }
@@ -653,9 +664,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
         for (int t = 0; t < w.ntiles; ++t, ++g) {
-          const uint32_t s = g % kSlots;
-          if (!(ok = wait_warp(bar(kVFull0 + s), (g / kSlots) & 1u, abort_flag))) break;
-          if (!(ok = wait_warp(bar(kPFull0 + s), (g / kSlots) & 1u, abort_flag))) break;
+          const uint32_t vs = g % kVStages, s = g % kPSlots;
+          if (!(ok = wait_warp(bar(kVFull0 + vs), (g / kVStages) & 1u, abort_flag))) break;
+          if (!(ok = wait_warp(bar(kPFull0 + s), (g / kPSlots) & 1u, abort_flag))) break;
           const uint32_t slot = base + kOffSlot + s * kSlotBytes;
           // re-arm the slot for its next message (sent only after this PV's credit)
           if (elect_one()) mbar_arrive_expect_tx(bar(kPFull0 + s), kMsgBytes);
@@ -671,7 +682,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             ++nresc;
           }
           if (t == 0 && it > 0 && !(ok = wait_warp(bar(kOFree), (it - 1) & 1u, abort_flag))) break;
-          const uint32_t vstage = base + kOffV + s * kVStage;
+          const uint32_t vstage = base + kOffV + vs * kVStage;
           if (elect_one()) {
             fence_proxy_async_smem();  // P arrived through st.async
             tc_fence_after();
@@ -684,7 +695,8 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
                 mma_bf16_ss(tmem + kTmemO + ch * 256, ad, bd, idesc_pv, (t == 0 && j == 0) ? 0u : 1u);
               }
             }
-            mma_commit_mc(bar(kSlotFree0 + s), (uint16_t)3);
+            mma_commit_mc(bar(kPSlotFree0 + s), (uint16_t)1);  // score CTA: P slot s is free
+            mma_commit(bar(kVFree0 + vs));                      // value stage vs is free
           }
           __syncwarp();
         }
@@ -696,11 +708,11 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         }
         __syncwarp();
       }
-    } else if (warp >= kSoftWarp0 && warp < kSoftWarp0 + kEpiWarps) {
+    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
       // ---- rescale requests and epilogue: one head row per thread, warp part
       // `part` of its lane quadrant owns O columns [cb0, cb1) ----
       const int quad = warp & 3;
-      const int part = (warp - kSoftWarp0) >> 2;
+      const int part = (warp - kEpiWarp0) >> 2;
       const int cb0 = 32 * epi_chunk0(part), cb1 = 32 * epi_chunk0(part + 1);
       const int row = quad * 32 + lane;
       const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
@@ -723,7 +735,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             const float alpha = *reinterpret_cast<const volatile float*>(slot + kAlphaOff + row * 4);
             // O is read and rescaled: the PV of tile g - 1 must be done
             const uint32_t gp = g - 1;
-            if (!(ok = wait_warp(bar(kSlotFree0 + gp % kSlots), (gp / kSlots) & 1u, abort_flag, true))) break;
+            if (!(ok = wait_warp(bar(kVFree0 + gp % kVStages), (gp / kVStages) & 1u, abort_flag))) break;
             tc_fence_after();
             uint32_t o[32];
 #pragma unroll 1
@@ -753,7 +765,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           mbar_arrive_remote(r_finfree0 + 8u * fb);
         }
         const uint32_t gl = g_end - 1;
-        if (!(ok = wait_warp(bar(kSlotFree0 + gl % kSlots), (gl / kSlots) & 1u, abort_flag, true))) break;
+        if (!(ok = wait_warp(bar(kVFree0 + gl % kVStages), (gl / kVStages) & 1u, abort_flag))) break;
         tc_fence_after();
         const size_t orow = (size_t)w.token * kPrHeads + row;
         if (p.split == 1) {
