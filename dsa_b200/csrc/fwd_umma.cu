@@ -66,6 +66,7 @@ constexpr uint32_t kOffK = kOffQ + kQBytes;
 constexpr uint32_t kOffP = kOffK + kUmStages * kKStage;      // P: 2 x (128 rows x 32 keys, SW64)
 constexpr uint32_t kPBytes = 128u * (uint32_t)kUmBN * 2u;    // 8192 per buffer
 constexpr uint32_t kOffMask = kOffP + 2u * kPBytes;          // validity bits per stage
+constexpr uint32_t kOffStageTile = kOffMask + 16u;           // tile index each stage is being filled with
 constexpr uint32_t kOffBar = kOffMask + 64u;
 
 enum Bar {
@@ -93,6 +94,7 @@ static_assert(kOffK % 1024 == 0 && kKStage % 1024 == 0 && kOffP % 1024 == 0, "sw
 static_assert(kTmemQ + kQTmemDims / 2 == kTmemCols, "TMEM budget");
 static_assert(kQTmemDims % 64 == 0, "Q TMEM part is a whole number of 64-dim blocks");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kOffStageTile + 4u * kUmStages <= kOffBar, "stage tile words");
 
 struct Item {
   int token, sp, half, batch, kbeg, kend, ntiles;
@@ -159,6 +161,30 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
+// Bounded wait (lane 0 polls) until a shared word equals `value`; the same
+// result in every lane.
+__device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t value, volatile int* abort) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0 && *word != value) {
+    const unsigned long long start = global_ns();
+    for (uint32_t k = 1; *word != value; ++k) {
+      if ((k & 15u) == 0) {
+        if (*abort) {
+          ok = false;
+          break;
+        }
+        if (global_ns() - start > kWaitLimitNs) {
+          *abort = 1;
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -176,6 +202,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     }
     mbar_init(bar(kQFull), kSoftWarps);
     mbar_init(bar(kQSeen), kQkIssuers);
+    for (int s = 0; s < kUmStages; ++s) reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = 0xffffffffu;
     for (int k = 0; k < kQkIssuers; ++k) {
       mbar_init(bar(kSFull0 + k), 1);
       mbar_init(bar(kSFree0 + k), kSoftWarps);
@@ -226,7 +253,11 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       }
       const int row = min(max(idx_cur, 0), L - 1);  // clamped address; masked below
       const uint32_t bits = __ballot_sync(0xffffffffu, (idx_cur >= 0) & (idx_cur < L));
-      if (lane == 0) *mask_s = bits;
+      if (lane == 0) {
+        *mask_s = bits;
+        // the stage's previous tile (g - 4) is consumed, so its Full phase completed
+        reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = s + kUmStages * n;
+      }
       const __nv_bfloat16* const kv_b = p.kv + (size_t)cur.w.batch * L * kDimLatent;
       const __nv_bfloat16* const kr_b = p.k_rope + (size_t)cur.w.batch * L * kDimRope;
 #pragma unroll 2
@@ -273,7 +304,12 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
         if (g % kQkIssuers != i) continue;
         const uint32_t s = g % kUmStages;
-        ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
+        // Issuer g % 3 has not observed the Full phase of the stage's previous
+        // tile (g - 4, another issuer's). Once the gather of tile g has
+        // started, that phase has completed and the parity wait refers to
+        // tile g's phase exactly.
+        ok = wait_word_warp(reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile) + s, g, abort_flag);
+        if (ok) ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
         if (ok && n > 0) ok = wait_warp(bar(kSFree0 + i), (n - 1) & 1u, abort_flag);
         if (!ok) break;
         tc_fence_after();
