@@ -128,7 +128,9 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
     const int64_t halves = 2 * batch * queries;
     const int64_t tiles = (topk + 31) / 32;
     int64_t split = ctas / halves;  // one wave: at most one item per resident CTA
-    if (split > tiles) split = tiles;
+    // at least two tiles per item: a one-tile item is all start-up (Q load,
+    // first gather, epilogue) and doubles the partials the merge reads
+    if (split > tiles / 2) split = tiles / 2;
     if (split < 1) split = 1;
     e.split = (int32_t)split;
     *out = e;

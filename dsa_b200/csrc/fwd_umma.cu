@@ -27,7 +27,11 @@
 // Warp roles (12 warps): 0-3 gather (warp w owns stage w: 16-byte cp.async of
 // the indexed rows into swizzled K-major tiles plus a validity bitmask);
 // 4-6 issue the QK MMAs; 7 issues the PV MMAs; 8-11 run the softmax, one head
-// row per thread, load Q per item and write the output. The online softmax
+// row per thread, and load Q per item. The epilogue of an item (O of the
+// item's last PV -> output or FP32 partial) runs in eight warps: the softmax
+// warp of each TMEM lane quadrant writes columns 0..127 of its 32 head rows
+// and the issuer warp of the same quadrant (4-7, idle at the item boundary)
+// columns 128..255. The online softmax
 // keeps the reference's semantics (dsa/workspace.py:242-318): invalid index
 // -> -inf, FP32 max/sum, BF16 P, FP32 O. O is only rescaled when the row max
 // grows by more than 2^8 in exp2 units (lazy rescale); the reported max is
@@ -67,7 +71,8 @@ constexpr uint32_t kOffP = kOffK + kUmStages * kKStage;      // P: 2 x (128 rows
 constexpr uint32_t kPBytes = 128u * (uint32_t)kUmBN * 2u;    // 8192 per buffer
 constexpr uint32_t kOffMask = kOffP + 2u * kPBytes;          // validity bits per stage
 constexpr uint32_t kOffStageTile = kOffMask + 16u;           // tile index each stage is being filled with
-constexpr uint32_t kOffBar = kOffMask + 64u;
+constexpr uint32_t kOffEpi = kOffMask + 64u;                  // (l, f) per head row for the epilogue
+constexpr uint32_t kOffBar = kOffEpi + (uint32_t)kUmHeads * 8u;
 
 enum Bar {
   kFull0 = 0,
@@ -78,7 +83,9 @@ enum Bar {
   kSFree0 = kSFull0 + kQkIssuers,
   kPFull0 = kSFree0 + kQkIssuers,  // P buffer b written (tiles g with g % 2 == b)
   kPvDone0 = kPFull0 + 2,          // PV of tiles g with g % 2 == b done (P buffer b free)
-  kBarCount = kPvDone0 + 2
+  kEpiGo = kPvDone0 + 2,           // the item's last PV is done and (l, f) are posted (softmax warps)
+  kOFree,                          // the QK issuers have read their part of O (next item's PV may start)
+  kBarCount
 };
 constexpr uint32_t kOffTmemSlot = kOffBar + kBarCount * 8u;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 8u;
@@ -94,7 +101,8 @@ static_assert(kOffK % 1024 == 0 && kKStage % 1024 == 0 && kOffP % 1024 == 0, "sw
 static_assert(kTmemQ + kQTmemDims / 2 == kTmemCols, "TMEM budget");
 static_assert(kQTmemDims % 64 == 0, "Q TMEM part is a whole number of 64-dim blocks");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert(kOffStageTile + 4u * kUmStages <= kOffBar, "stage tile words");
+static_assert(kOffStageTile + 4u * kUmStages <= kOffEpi, "stage tile words");
+static_assert(kQkIssuers + 1 == 4 && kQkWarp0 % 4 == 0, "one issuer warp per TMEM lane quadrant");
 
 struct Item {
   int token, sp, half, batch, kbeg, kend, ntiles;
@@ -185,6 +193,49 @@ __device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+// Columns [cb0, cb1) (multiples of 32) of O for this thread's head row (TMEM
+// lane `o_lane`) -> the output (O / l as BF16, split 1) or the FP32 partial
+// (O * f); two 32-column chunks in flight so each load overlaps a store.
+__device__ __forceinline__ void store_o_part(const FwdParams& p, const Item& w, uint32_t o_lane, int row, int cb0,
+                                             int cb1, float l, float f) {
+  uint32_t oa[32], ob[32];
+  const int col0 = w.half * 256;
+  if (p.split == 1) {
+    // correctly rounded reciprocal (within an FP32 ulp of O / l); a row
+    // without a valid index (l == 0) is written as 0
+    const float rl = l > 0.f ? __frcp_rn(l) : 0.f;
+    __nv_bfloat16* dst = p.out + ((size_t)w.token * kUmHeads + row) * kDimLatent + col0;
+    const bool wide = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;  // rows are 1024 B apart
+    tmem_ld32(o_lane + cb0, oa);
+#pragma unroll 1
+    for (int cb = cb0; cb < cb1; cb += 64) {
+      tmem_wait_ld_regs32(oa);
+      const bool more = cb + 32 < cb1;
+      if (more) tmem_ld32(o_lane + cb + 32, ob);
+      store_bf16_row32(dst + cb, oa, rl, wide);
+      if (!more) break;
+      tmem_wait_ld_regs32(ob);
+      if (cb + 64 < cb1) tmem_ld32(o_lane + cb + 64, oa);
+      store_bf16_row32(dst + cb + 32, ob, rl, wide);
+    }
+  } else {
+    float* dst = p.part_num + (((size_t)w.token * p.split + w.sp) * kUmHeads + row) * kDimLatent + col0;
+    const bool wide = (reinterpret_cast<uintptr_t>(p.part_num) & 31u) == 0;  // rows are 2048 B apart
+    tmem_ld32(o_lane + cb0, oa);
+#pragma unroll 1
+    for (int cb = cb0; cb < cb1; cb += 64) {
+      tmem_wait_ld_regs32(oa);
+      const bool more = cb + 32 < cb1;
+      if (more) tmem_ld32(o_lane + cb + 32, ob);
+      store_f32_row32(dst + cb, oa, f, wide);
+      if (!more) break;
+      tmem_wait_ld_regs32(ob);
+      if (cb + 64 < cb1) tmem_ld32(o_lane + cb + 64, oa);
+      store_f32_row32(dst + cb + 32, ob, f, wide);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -211,6 +262,8 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       mbar_init(bar(kPFull0 + b), kSoftWarps);
       mbar_init(bar(kPvDone0 + b), 1);
     }
+    mbar_init(bar(kEpiGo), kSoftWarps);
+    mbar_init(bar(kOFree), kQkIssuers);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -225,6 +278,19 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
 
   const int n_items = p.tokens * p.split * 2;
   const int L = p.length;
+  float2* const epi = reinterpret_cast<float2*>(sbase + kOffEpi);
+  // Columns 128..255 of O for the item's head rows in TMEM lane quadrant
+  // warp % 4, by an issuer warp once the softmax warps post the item's (l, f).
+  auto epilogue_upper_half = [&](const Item& w, uint32_t it) -> bool {
+    if (!wait_warp(bar(kEpiGo), it & 1u, abort_flag)) return false;
+    tc_fence_after();
+    const int row = (warp & 3) * 32 + lane;
+    const float2 lf = epi[row];
+    store_o_part(p, w, tmem + ((uint32_t)((warp & 3) * 32) << 16) + kTmemO, row, 128, 256, lf.x, lf.y);
+    tc_fence_before();
+    __syncwarp();
+    return true;
+  };
 
   if (warp < kGatherWarps) {
     // ---------------- gather: warp w fills stage w for tiles g = w, w+4, ... ----------------
@@ -335,18 +401,23 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         __syncwarp();
         ++n;
       }
+      if (!ok || !(ok = epilogue_upper_half(w, it))) break;
+      if (lane == 0) mbar_arrive(bar(kOFree));
     }
     if (!ok && lane == 0) report_error(p.status, kErrTimeout);
   } else if (warp == kPvWarp) {
     // ---------------- PV issuer: every tile in order (warp-converged, one elected lane issues) ----
     const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
-    uint32_t g = 0;
+    uint32_t g = 0, it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
       const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
       for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
         ok = wait_warp(bar(kPFull0 + (g & 1u)), (g >> 1) & 1u, abort_flag);
+        // the first PV of an item overwrites O: the previous item's epilogue
+        // (the QK issuers' part) must have read it
+        if (ok && t == 0 && it > 0) ok = wait_warp(bar(kOFree), (it - 1) & 1u, abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t stage = base + kOffK + (g % kUmStages) * kKStage;
@@ -362,6 +433,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         }
         __syncwarp();
       }
+      if (!ok || !(ok = epilogue_upper_half(w, it))) break;
     }
     if (!ok && lane == 0) report_error(p.status, kErrTimeout);
   } else {
@@ -502,52 +574,28 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         if (lane == 0) mbar_arrive(bar(kPFull0 + pb));
       }
       if (!ok) break;
-      // ---- epilogue: this CTA's 256 dims of the head row -> output (or FP32 partial) ----
+      // ---- epilogue: columns 0..127 of this CTA's 256 dims of the head row
+      // (the issuer warp of this lane quadrant writes 128..255) ----
       ok = wait_warp(bar(kPvDone0 + ((g - 1) & 1u)), ((g - 1) >> 1) & 1u, abort_flag);
       if (!ok) break;
-      tc_fence_after();
       const float f = (m_true == kNegFltMax) ? 1.f : ex2((m_used - m_true) * c);
+      epi[row] = make_float2(l, f);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kEpiGo));
+      tc_fence_after();
       const size_t orow = (size_t)w.token * kUmHeads + row;
-      const int col0 = w.half * 256;
-      if (p.split == 1) {
-        const float ld = l > 0.f ? l : INFINITY;  // a row without a valid index is written as 0
-        __nv_bfloat16* dst = p.out + orow * kDimLatent + col0;
-#pragma unroll 1
-        for (int cb = 0; cb < 256; cb += 32) {
-          uint32_t o[32];
-          tmem_ld32(tmem + t_lane + kTmemO + cb, o);
-          tmem_wait_ld();
-          uint32_t h[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            h[k] = pack_bf16x2(__fdiv_rn(u2f(o[2 * k]), ld), __fdiv_rn(u2f(o[2 * k + 1]), ld));
-          uint4* d4 = reinterpret_cast<uint4*>(dst + cb);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
-        }
-        if (w.half == 0) {
+      if (w.half == 0) {
+        if (p.split == 1) {
           p.out_max[orow] = final_max(m_true, l, p.scale_div);
           p.out_sum[orow] = l * f;
-        }
-      } else {
-        const size_t prow_idx = ((size_t)w.token * p.split + w.sp) * kUmHeads + row;
-        float* dst = p.part_num + prow_idx * kDimLatent + col0;
-#pragma unroll 1
-        for (int cb = 0; cb < 256; cb += 32) {
-          uint32_t o[32];
-          tmem_ld32(tmem + t_lane + kTmemO + cb, o);
-          tmem_wait_ld();
-          float4* d4 = reinterpret_cast<float4*>(dst + cb);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            d4[k] = make_float4(u2f(o[4 * k]) * f, u2f(o[4 * k + 1]) * f, u2f(o[4 * k + 2]) * f,
-                                u2f(o[4 * k + 3]) * f);
-        }
-        if (w.half == 0) {
+        } else {
+          const size_t prow_idx = ((size_t)w.token * p.split + w.sp) * kUmHeads + row;
           p.part_max[prow_idx] = (m_true == kNegFltMax) ? kNegFltMax : __fdiv_rn(m_true, p.scale_div);
           p.part_sum[prow_idx] = l * f;
         }
       }
+      store_o_part(p, w, tmem + t_lane + kTmemO, row, 0, 128, l, f);
       tc_fence_before();
     }
     if (!ok) report_error(p.status, kErrTimeout);

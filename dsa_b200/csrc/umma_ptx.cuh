@@ -297,5 +297,46 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn_major,
          ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// ---- row stores of the epilogues -------------------------------------------------------
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* h) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+               "r"(h[3]), "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7])
+               : "memory");
+}
+
+// 32 FP32 values (O columns of one head row) * rl -> 32 BF16 at dst (64 B).
+// Each thread writes its own row, so a warp store touches 32 rows: 32-byte
+// stores (whole L2 sectors, half the requests of 16-byte ones) when dst is
+// 32-byte aligned (`wide`), 16-byte stores otherwise.
+__device__ __forceinline__ void store_bf16_row32(__nv_bfloat16* dst, const uint32_t* o, float rl, bool wide) {
+  uint32_t h[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) h[k] = pack_bf16x2(__uint_as_float(o[2 * k]) * rl, __uint_as_float(o[2 * k + 1]) * rl);
+  if (wide) {
+    st_global_v8(dst, h);
+    st_global_v8(dst + 16, h + 8);
+  } else {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+  }
+}
+
+// 32 FP32 values * f -> dst (128 B of an FP32 partial row); 32-byte stores
+// when dst is 32-byte aligned (`wide`), 16-byte stores otherwise.
+__device__ __forceinline__ void store_f32_row32(float* dst, const uint32_t* o, float f, bool wide) {
+  uint32_t h[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) h[k] = __float_as_uint(__uint_as_float(o[k]) * f);
+  if (wide) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) st_global_v8(dst + 8 * k, h + 8 * k);
+  } else {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) d4[k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+  }
+}
+
 }  // namespace umma
 }  // namespace dsa
