@@ -26,6 +26,7 @@ FAMILY_WARP_MMA = 1
 FAMILY_UMMA = 2
 FAMILY_UMMA_PAIR = 3
 FAMILY_STREAM = 4
+FAMILY_KEYS = 5
 
 # Every entry point declared in include/dsa_b200.h.
 EXPORTS = (

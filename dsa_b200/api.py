@@ -24,7 +24,8 @@ DEVICE_TYPE = "cuda"
 LaunchRecord = namedtuple("LaunchRecord", "name family heads_per_cta keys_per_tile split")
 
 _FAMILY_NAMES = {_native.FAMILY_WARP_MMA: "warp_mma", _native.FAMILY_UMMA: "umma",
-                 _native.FAMILY_UMMA_PAIR: "umma_pair", _native.FAMILY_STREAM: "stream"}
+                 _native.FAMILY_UMMA_PAIR: "umma_pair", _native.FAMILY_STREAM: "stream",
+                 _native.FAMILY_KEYS: "keys"}
 
 
 def _check_inputs(q, kv, q_rope, k_rope, indices):
@@ -96,6 +97,8 @@ def _launch_from_tuning(config, shape):
         launch = _native.Launch(family, 128, config.bn, config.split)
     elif config.bn == 32:
         launch = _native.Launch(_native.FAMILY_STREAM, 16, config.bn, config.split)
+    elif config.pv_cols == 128:
+        launch = _native.Launch(_native.FAMILY_KEYS, 16, config.bn, config.split)
     else:
         launch = _native.Launch(_native.FAMILY_WARP_MMA, 16, config.bn, config.split)
     code = _native.load().dsa_check_launch(*shape, ctypes.byref(launch))

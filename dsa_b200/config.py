@@ -10,13 +10,17 @@ B200:
 * ``bm`` — heads that share one gathered KV tile. ``bm == 128`` selects a
   tcgen05/TMEM family for H = 128; any other legal ``bm`` selects a 16-head
   family (each CTA item owns 16 heads).
-* ``bn`` — selected KV rows per pipeline stage: 32 (tcgen05 families and the
-  persistent stream family for ``bm < 128``) or 64 (the warp-MMA family).
+* ``bn`` — selected KV rows per pipeline stage: 32 (tcgen05 families for
+  ``bm == 128`` and the persistent stream family for ``bm < 128``) or 64 (the
+  warp-MMA and keys families).
 * ``split`` — KV splits per (query, head tile); ``split > 1`` writes FP32
   partials to the workspace and runs the FP32 merge (dsa/merge.py).
 * ``pv_cols`` — value columns one CTA accumulates, for ``bm == 128``: 512
   selects the pair family (score CTA + value CTA per query), 256 the split-V
-  family (two CTAs per query, each over half of the 512 columns).
+  family (two CTAs per query, each over half of the 512 columns). For
+  ``bm < 128, bn == 64``, 128 selects the keys family (tcgen05 with the
+  selected keys as the MMA's M dimension and the value product computed in
+  128-column blocks) instead of the warp-MMA family.
 * ``direct_nz``, ``share_score`` — Ascend data-movement knobs (NZ packing,
   score/PV UB sharing) with no counterpart on sm_100a. They are type-checked
   as in the reference but do not change the launch.

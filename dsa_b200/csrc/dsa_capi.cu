@@ -88,6 +88,10 @@ int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t leng
       if (launch->heads_per_cta != 16 || heads % 16 != 0 || bn != 32) return DSA_STATUS_UNSUPPORTED;
       break;
     }
+    case DSA_FAMILY_KEYS: {
+      if (launch->heads_per_cta != 16 || heads % 16 != 0 || bn != 64) return DSA_STATUS_UNSUPPORTED;
+      break;
+    }
     case DSA_FAMILY_UMMA:
     case DSA_FAMILY_UMMA_PAIR: {
       if (launch->heads_per_cta != 128 || heads != 128 || bn != 32) return DSA_STATUS_UNSUPPORTED;
@@ -224,6 +228,7 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
     case DSA_FAMILY_UMMA: err = dsa::launch_fwd_umma(p, s); break;
     case DSA_FAMILY_UMMA_PAIR: err = dsa::launch_fwd_pair(p, s); break;
     case DSA_FAMILY_STREAM: err = dsa::launch_fwd_stream(p, s); break;
+    case DSA_FAMILY_KEYS: err = dsa::launch_fwd_keys(p, s); break;
     default: return DSA_STATUS_UNSUPPORTED;
   }
   if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;

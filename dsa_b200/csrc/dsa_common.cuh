@@ -149,8 +149,10 @@ cudaError_t launch_fwd_pair(const FwdParams& p, cudaStream_t stream);
 // CTAs of the pair family (two per cluster) resident at once (-1 on error).
 int pair_max_ctas();
 cudaError_t launch_fwd_stream(const FwdParams& p, cudaStream_t stream);
+cudaError_t launch_fwd_keys(const FwdParams& p, cudaStream_t stream);
 // CTAs of the stream family resident at once (-1 on error).
 int stream_max_ctas();
+int keys_max_ctas();
 cudaError_t launch_merge(const float* num, const float* pmax, const float* psum,
                          __nv_bfloat16* out, float* omax, float* osum, int tokens, int heads,
                          int split, cudaStream_t stream);

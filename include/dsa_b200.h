@@ -74,8 +74,11 @@ typedef enum dsa_family {
                                value columns); each CTA computes the full scores */
   DSA_FAMILY_UMMA_PAIR = 3, /* tcgen05/TMEM path, H == 128: a 2-CTA cluster per query, one CTA
                                computes scores + softmax, the other P.V over all 512 columns */
-  DSA_FAMILY_STREAM = 4     /* persistent warp-level MMA, 16 heads per CTA item, gather warps keep
+  DSA_FAMILY_STREAM = 4,    /* persistent warp-level MMA, 16 heads per CTA item, gather warps keep
                                the selected rows in flight; any H % 16 == 0, keys_per_tile 32 */
+  DSA_FAMILY_KEYS = 5       /* persistent tcgen05/TMEM path for 16 heads per CTA item with the
+                               selected keys as the MMA's M dimension (scores and P.V computed
+                               transposed); any H % 16 == 0, keys_per_tile 64 */
 } dsa_family_t;
 
 /* One entry of the shape-keyed launch table (reference: Tuning,

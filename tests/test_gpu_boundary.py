@@ -9,10 +9,11 @@ from oracle import sparse_mla as oracle
 
 pytestmark = pytest.mark.gpu
 
-# (heads, Tuning) per family: warp-MMA, stream, split-V (tcgen05), pair (tcgen05)
+# (heads, Tuning) per family: warp-MMA, stream, keys (tcgen05), split-V (tcgen05), pair (tcgen05)
 FAMILIES = {
     "warp_mma": (32, lambda split: dsa_b200.Tuning(16, 64, split)),
     "stream": (32, lambda split: dsa_b200.Tuning(16, 32, split)),
+    "keys": (32, lambda split: dsa_b200.Tuning(16, 64, split, pv_cols=128)),
     "splitv": (128, lambda split: dsa_b200.Tuning(128, 32, split, pv_cols=256)),
     "pair": (128, lambda split: dsa_b200.Tuning(128, 32, split, pv_cols=512)),
 }

@@ -58,6 +58,10 @@ def test_check_launch_rejections():
         e = _native.Launch(fam, bm, bn, split)
         assert lib.dsa_check_launch(*shape, ctypes.byref(e)) != 0, (fam, bm, bn, split)
     assert lib.dsa_check_launch(1, 1, 24, 1024, 256, ctypes.byref(_native.Launch(1, 16, 32, 1))) != 0
+    # keys family: 64-key tiles only
+    assert lib.dsa_check_launch(*shape, ctypes.byref(_native.Launch(_native.FAMILY_KEYS, 16, 64, 4))) == 0
+    assert lib.dsa_check_launch(*shape, ctypes.byref(_native.Launch(_native.FAMILY_KEYS, 16, 32, 1))) != 0
+    assert lib.dsa_check_launch(*shape, ctypes.byref(_native.Launch(_native.FAMILY_KEYS, 16, 64, 5))) != 0
     assert lib.dsa_check_launch(0, 1, 32, 1024, 256, ctypes.byref(_native.Launch(1, 16, 32, 1))) != 0
 
 
