@@ -52,9 +52,12 @@ DEFAULT_CONFIG = "prefill_h128"
 # dram__bytes_write.sum) from the ncu captures summarised under profiles/;
 # None until a capture of that kernel/config exists.
 TRAFFIC_BYTES = {
-    # profiles/fwd_pair_prefill_h128.md: 394.4 MB (DRAM read + write) for a
-    # 512-query capture of fwd_pair_kernel, scaled to 16384 queries.
-    "prefill_h128": int(394.4e6 * 16384 / 512),
+    # profiles/fwd_pair_prefill_h128.md: 356.9 + 59.3 MB (DRAM read + write)
+    # for a 512-query capture of fwd_pair_kernel, scaled to 16384 queries.
+    "prefill_h128": int((356.9e6 + 59.3e6) * 16384 / 512),
+    # profiles/fwd_umma_decode_b8.md: 39.07 MB + 0.45 MB, a capture of the
+    # full decode_b8 launch of fwd_umma_kernel.
+    "decode_b8": int(39.07e6 + 0.45e6),
 }
 
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
