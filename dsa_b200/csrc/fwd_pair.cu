@@ -9,7 +9,8 @@
 //                                           A = Q held in TMEM (all 576 dims)
 //                       P = bf16(exp(S/24 - m)), FP32 online softmax (thread = head row)
 //                       P, the per-row rescale factor and a per-warp rescale flag are
-//                       written into the value CTA's shared memory with st.async
+//                       staged in the score CTA's shared memory and copied into the
+//                       value CTA's with one bulk copy per tile
 //   value CTA (rank 1)  O += P . V          tcgen05, M=128, N=2x256, K=32 keys,
 //                                           O (128 x 512 FP32) fills the whole TMEM
 //
@@ -28,20 +29,25 @@
 // split partials are rescaled to it at the end.
 //
 // Roles (20 warps per CTA):
-//   score CTA: 0-5 gather (warp w owns stage w: 16-byte cp.async of the full
-//              rows into 128-byte-swizzled K-major tiles), 8-15 softmax: two
-//              warps per TMEM lane quadrant (head rows 32q..32q+31), warp 8+q
-//              takes the even tiles and warp 12+q the odd ones. The running
+//   score CTA: 0-4 gather (warp w owns stage w: 16-byte cp.async of the full
+//              rows into 128-byte-swizzled K-major tiles), 5 P sender (one
+//              bulk shared-to-shared copy per tile from a local staging slot
+//              to the value CTA's P slot, so the softmax warps only write
+//              their own shared memory: cross-SM stores issued by the
+//              softmax warps themselves held them ~0.3 us per tile), 6-13
+//              softmax: two warps per TMEM lane quadrant (head rows
+//              32q..32q+31), the warp of quadrant q among 6-9 / 10-13
+//              takes the even / odd tiles. The running
 //              max is the only dependence between consecutive tiles: a warp
 //              posts the max it used for its tile (one bounded mbarrier phase
 //              per tile) right after its row-max reduction, and the other warp
 //              waits for it before deciding its own, so the exponentials and
 //              the P transfer of consecutive tiles overlap. Key validity comes
 //              from the indices (loaded a tile ahead), so a stage is free as
-//              soon as its QK MMAs complete. 16-19 QK issuers (tile g ->
-//              issuer g % 4: issuing a tcgen05.mma occupies the issuing warp's
-//              scheduler, so the 36 MMAs of each tile are spread over the four
-//              schedulers) into S buffer g % 4 (a buffer returns to the
+//              soon as its QK MMAs complete. 14-19 QK issuers (tile g ->
+//              issuer g % 6: issuing a tcgen05.mma occupies the issuing warp's
+//              scheduler, so the 36 MMAs of each tile are spread over the
+//              schedulers) into S buffer g % 6 (a buffer returns to the
 //              issuers only after its softmax read). At an
 //              item boundary the issuers also load three of the nine Q chunks
 //              of their lane quadrant, and the next item's Q is prefetched
@@ -60,11 +66,16 @@ using namespace umma;
 
 constexpr int kPrBN = 32;       // keys per tile
 constexpr int kPrHeads = 128;
-// Tile g of the cluster's sequence uses stage, S buffer and P slot g % 6,
-// gather warp and QK issuer g % 6 and softmax warp g % 2 of each lane
-// quadrant: every mbarrier is waited on by one role whose consecutive waits
-// on it are one phase apart, the condition for parity waits to be exact.
-constexpr int kKStages = 6;     // score CTA: gathered full rows (gather warp w owns stage w)
+// Tile g of the cluster's sequence uses S buffer and P slot g % 6, QK issuer
+// g % 6, stage and gather warp g % 5, local staging slot g % 4 and softmax
+// warp g % 2 of each lane quadrant: every mbarrier is waited on by one role
+// whose consecutive waits on it are one phase apart, the condition for
+// parity waits to be exact. The one exception, a QK issuer waiting for the
+// stage g % 5 of its tile g % 6, first waits until the gather warp has
+// started that tile (a per-stage tile word), which fixes the phase.
+constexpr int kKStages = 5;     // score CTA: gathered full rows (gather warp w owns stage w)
+constexpr int kLSlots = 4;      // score CTA: local P staging slots (even: slot g % 4 is always softmax warp g % 2's)
+constexpr int kSendWarp = kKStages;  // score CTA: warp 5 sends the staged P
 constexpr int kSBufs = 6;       // score CTA: S accumulators in TMEM
 constexpr int kQkIssuers = 6;   // score CTA: QK issuer i takes tiles g = i mod 6
 constexpr int kQkQHelpers = 4;  // issuers 0-3 also load Q chunks of their lane quadrant
@@ -72,7 +83,7 @@ constexpr int kVStages = 5;     // value CTA: gathered value rows
 constexpr int kPSlots = 6;      // value CTA: P slots
 constexpr int kPrThreads = 640;
 constexpr int kPvWarp = 6;      // value CTA: gather 0-4, PV issuer 6, rescale+epilogue 8-19
-constexpr int kSoftWarp0 = 6;   // score CTA: gather 0-5, softmax 6-13, QK issuers 14-19
+constexpr int kSoftWarp0 = 6;   // score CTA: gather 0-4, sender 5, softmax 6-13, QK issuers 14-19
 constexpr int kSoftWarps = 8;
 constexpr int kEpiWarp0 = 8;
 constexpr int kEpiWarps = 12;   // value CTA: warps 8..19, three per TMEM lane quadrant
@@ -106,8 +117,10 @@ enum Bar {
   kXchg0 = kFinFree0 + 2,           // 4: per lane quadrant, both softmax warps posted their item totals
   kMReady0 = kXchg0 + 4,            // 4: per lane quadrant, the running max of the latest tile is posted
   kPSlotFree0 = kMReady0 + 4,       // P slot's PV done (commit multicast from the value CTA)
+  kLFull0 = kPSlotFree0 + kPSlots,  // local staging slot written (the tile's 4 softmax warps)
+  kLFree0 = kLFull0 + kLSlots,      // local staging slot read by its bulk copy (sender)
   // value CTA
-  kVFull0 = kPSlotFree0 + kPSlots,
+  kVFull0 = kLFree0 + kLSlots,
   kVFree0 = kVFull0 + kVStages,     // value stage's PV done
   kPFull0 = kVFree0 + kVStages,     // P message landed (complete_tx)
   kReq = kPFull0 + kPSlots,         // a rescale or epilogue request is posted
@@ -120,13 +133,14 @@ constexpr uint32_t kOffBar = 0;
 constexpr uint32_t kOffTmemSlot = kOffBar + kBarCount * 8u;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 8u;
 constexpr uint32_t kOffReq = kOffAbort + 8u;
-constexpr uint32_t kOffMask = kOffReq + 8u;             // score CTA: one word per stage
+constexpr uint32_t kOffStageTile = kOffReq + 8u;        // score CTA: tile each stage is being filled with
 constexpr uint32_t kOffData = 1024u;
 constexpr uint32_t kOffK = kOffData;                     // score CTA stages
 constexpr uint32_t kOffV = kOffData;                     // value CTA stages
 constexpr uint32_t kOffSlot = kOffV + kVStages * kVStage;  // value CTA P slots
 constexpr uint32_t kOffFin = kOffSlot + kPSlots * kSlotBytes;
-constexpr uint32_t kOffX = kOffK + kKStages * kKStage;   // score CTA: [2][4 quads][2 warps][3][32] floats
+constexpr uint32_t kOffLocal = kOffK + kKStages * kKStage;  // score CTA: P staging slots
+constexpr uint32_t kOffX = kOffLocal + kLSlots * kSlotBytes;  // score CTA: [2][4 quads][2 warps][3][32] floats
 constexpr uint32_t kOffM = kOffX + 2u * 4u * 2u * 3u * 32u * 4u;  // score CTA: [2][4 quads][32] running maxima
 constexpr uint32_t kSmemScore = kOffM + 2u * 4u * 32u * 4u;
 constexpr uint32_t kSmemValue = kOffFin + 2u * kFinBytes;
@@ -140,7 +154,9 @@ constexpr uint32_t kTmemQ = 0;      // score CTA: Q, 288 columns (dims 0..575 as
 constexpr uint32_t kTmemS = 288;    // score CTA: S buffers, 32 columns each
 constexpr uint32_t kTmemO = 0;      // value CTA: O, 512 columns
 
-static_assert(kOffMask + 4u * kKStages <= kOffData, "barrier block");
+static_assert(kOffStageTile + 4u * kKStages <= kOffData, "barrier block");
+static_assert(kLSlots % 2 == 0, "a staging slot must always belong to the same softmax warp");
+static_assert(kOffLocal % 1024 == 0 && kMsgBytes % 16 == 0, "bulk copy alignment");
 static_assert(kOffSlot % 1024 == 0 && kSlotBytes % 1024 == 0, "P slots are 1024-aligned");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kTmemS + kSBufs * kPrBN <= kTmemCols, "score TMEM budget");
@@ -209,23 +225,10 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
-__device__ __forceinline__ void st_async_b32x4(uint32_t remote_addr, uint32_t remote_bar, uint32_t a, uint32_t b,
-                                               uint32_t c, uint32_t d) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-          remote_addr),
-      "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
-      : "memory");
-}
 __device__ __forceinline__ void st_async_b32x2(uint32_t remote_addr, uint32_t remote_bar, uint32_t a, uint32_t b) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(
                    remote_addr),
                "r"(a), "r"(b), "r"(remote_bar)
-               : "memory");
-}
-__device__ __forceinline__ void st_async_b32(uint32_t remote_addr, uint32_t remote_bar, uint32_t a) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote_addr),
-               "r"(a), "r"(remote_bar)
                : "memory");
 }
 // Arrive once on the barrier at `bar`'s offset in every CTA of `cta_mask`
@@ -308,6 +311,12 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         mbar_init(bar(kMReady0 + q), 1);
       }
       for (int s = 0; s < kPSlots; ++s) mbar_init(bar(kPSlotFree0 + s), 1);
+      for (int s = 0; s < kLSlots; ++s) {
+        mbar_init(bar(kLFull0 + s), 4);
+        mbar_init(bar(kLFree0 + s), 1);
+      }
+      for (int s = 0; s < kKStages; ++s)
+        reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = 0xffffffffu;
     } else {
       for (int s = 0; s < kVStages; ++s) {
         mbar_init(bar(kVFull0 + s), 1);
@@ -344,7 +353,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
   if (rank == 0) {
     // =============================== score CTA ===============================
     if (warp < kKStages) {
-      // ---- gather: warp w fills stage w for tiles g = w, w+6, ... ----
+      // ---- gather: warp w fills stage w for tiles g = w, w+5, ... ----
       const uint32_t s = (uint32_t)warp;
       const uint32_t stage = base + kOffK + s * kKStage;
       PCursor cur = pcursor_start(p, n_items, cid, ncl, (int)s);
@@ -357,6 +366,8 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       uint32_t n = 0;
       while (cur.item < n_items) {
         if (n > 0 && !(ok = wait_warp(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag))) break;
+        // the stage's previous tile (g - 5) is consumed, so its Full phase completed
+        if (lane == 0) reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = s + kKStages * n;
         const int row = min(max(idx_cur, 0), L - 1);  // clamped address; masked by the softmax
         gather_rows(stage, p.kv + (size_t)cur.w.batch * L * kDimLatent,
                     p.k_rope + (size_t)cur.w.batch * L * kDimRope, row, lane, true);
@@ -374,7 +385,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         idx_nx = idx_nx2;
       }
     } else if (warp >= kQkWarp0 && warp < kQkWarp0 + kQkIssuers) {
-      // ---- QK issuer i: S buffer g % 6 <- Q (TMEM) . K^T (stage g % 6) for tiles g = i mod 6 ----
+      // ---- QK issuer i: S buffer g % 6 <- Q (TMEM) . K^T (stage g % 5) for tiles g = i mod 6 ----
       const uint32_t i = (uint32_t)(warp - kQkWarp0);
       const uint32_t idesc_qk = idesc_bf16(128, kPrBN, false, false);
       uint32_t g = 0, it = 0;
@@ -404,6 +415,12 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           if (g % kQkIssuers != i) continue;
           const uint32_t s = g % kKStages, b = g % kSBufs;
           const uint32_t d = tmem + kTmemS + b * kPrBN;
+          // this issuer has not observed the Full phase of the stage's previous
+          // tile (g - 5, another issuer's); once the gather of tile g has
+          // started, that phase has completed and the parity wait refers to
+          // tile g's phase exactly
+          if (!(ok = wait_word_warp(reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile) + s, g, abort_flag)))
+            break;
           if (!(ok = wait_warp(bar(kFull0 + s), (g / kKStages) & 1u, abort_flag))) break;
           // S buffer b was last used by tile g - 6 (this issuer's): its softmax has read it
           if (g >= kSBufs && !(ok = wait_warp(bar(kSFree0 + b), ((g / kSBufs) - 1) & 1u, abort_flag))) break;
@@ -422,6 +439,36 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           __syncwarp();
         }
       }
+    } else if (warp == kSendWarp) {
+      // ---- P sender: staging slot g % 4 -> the value CTA's P slot g % 6, one bulk copy per tile ----
+      const uint32_t r_slot0 = mapa_shared(base + kOffSlot, 1);
+      const uint32_t r_pfull0 = mapa_shared(bar(kPFull0), 1);
+      uint32_t g = 0;
+      for (int item = cid; item < n_items && ok; item += ncl) {
+        const PItem w = make_pitem(p, item);
+        for (int t = 0; t < w.ntiles; ++t, ++g) {
+          const uint32_t ls = g % kLSlots, ps = g % kPSlots;
+          if (!(ok = wait_warp(bar(kLFull0 + ls), (g / kLSlots) & 1u, abort_flag))) break;
+          // the value CTA's P slot ps is free once the PV of tile g - 6 is done
+          if (g >= kPSlots && !(ok = wait_warp(bar(kPSlotFree0 + ps), ((g / kPSlots) - 1) & 1u, abort_flag)))
+            break;
+          if (lane == 0) {
+            bulk_copy_to_peer(r_slot0 + ps * kSlotBytes, base + kOffLocal + ls * kSlotBytes, kMsgBytes,
+                              r_pfull0 + 8u * ps);
+            bulk_commit_group();
+            bulk_wait_group_read<1>();  // the copy of tile g - 1 has read its staging slot
+          }
+          __syncwarp();
+          if (g >= 1 && lane == 0) mbar_arrive(bar(kLFree0 + (g - 1) % kLSlots));
+        }
+      }
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+      // the value CTA's last P-slot credits (its PVs have read every copy)
+      for (uint32_t k = 0; ok && k < (uint32_t)kPSlots && k < g; ++k) {
+        const uint32_t gl = g - 1 - k;
+        ok = wait_warp(bar(kPSlotFree0 + gl % kPSlots), (gl / kPSlots) & 1u, abort_flag);
+      }
     } else if (warp >= kSoftWarp0 && warp < kSoftWarp0 + kSoftWarps) {
       // ---- softmax: head row per thread; warp e = 0 / 1 of the quadrant takes tiles g % 2 == e ----
       const int quad = warp & 3;
@@ -431,8 +478,6 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       const float c = p.scale_log2;  // log2(e) / scale_div
       float* const xch = reinterpret_cast<float*>(sbase + kOffX);  // [parity][quad][warp][3][lane]
       float* const mpub = reinterpret_cast<float*>(sbase + kOffM);  // [tile parity][quad][lane]
-      const uint32_t r_slot0 = mapa_shared(base + kOffSlot, 1);
-      const uint32_t r_pfull0 = mapa_shared(bar(kPFull0), 1);
       const uint32_t r_fin0 = mapa_shared(base + kOffFin, 1);
       const uint32_t r_finbar0 = mapa_shared(bar(kFin0), 1);
       // P row offset in a slot (SW64 K-major: 8-row groups of 512 B, 16-byte chunks swizzled)
@@ -474,7 +519,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             else
               prefetch_l2_bulk(p.q_rope + qn * kDimRope, 16384u);
           }
-          const uint32_t i = g % kSBufs, ps = g % kPSlots;
+          const uint32_t i = g % kSBufs;
           const int idx = idx_nxt;  // this tile's indices (loaded one tile ahead)
           pcursor_advance(p, n_items, ncl, nxt, 2);
           idx_nxt = pcursor_index(p, nxt, n_items, lane);
@@ -540,17 +585,20 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           }
           l += psum[0];
           const uint32_t flag = __any_sync(0xffffffffu, resc) ? 1u : 0u;
-          // P slot ps is free once the PV of tile g - 6 (this warp's) is done
-          if (g >= kPSlots && !(ok = wait_warp(bar(kPSlotFree0 + ps), ((g / kPSlots) - 1) & 1u, abort_flag)))
-            break;
-          const uint32_t slot = r_slot0 + ps * kSlotBytes;
-          const uint32_t pbar = r_pfull0 + 8u * ps;
+          // staging slot ls (this warp's) is free once the bulk copy of
+          // tile g - 4 has read it
+          const uint32_t ls = g % kLSlots;
+          if (g >= kLSlots && !(ok = wait_warp(bar(kLFree0 + ls), ((g / kLSlots) - 1) & 1u, abort_flag))) break;
+          uint8_t* const lslot = sbase + kOffLocal + ls * kSlotBytes;
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            st_async_b32x4(slot + prow + (uint32_t)((q ^ ((row & 7) >> 1)) * 16), pbar, packed[4 * q],
-                           packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          st_async_b32(slot + kAlphaOff + (uint32_t)row * 4u, pbar, f2u(alpha));
-          if (lane == 0) st_async_b32(slot + kFlagOff + (uint32_t)quad * 4u, pbar, flag);
+            *reinterpret_cast<uint4*>(lslot + prow + (uint32_t)((q ^ ((row & 7) >> 1)) * 16)) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          *reinterpret_cast<uint32_t*>(lslot + kAlphaOff + (uint32_t)row * 4u) = f2u(alpha);
+          if (lane == 0) *reinterpret_cast<uint32_t*>(lslot + kFlagOff + (uint32_t)quad * 4u) = flag;
+          fence_proxy_async_smem();  // generic-proxy writes -> visible to the bulk copy
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kLFull0 + ls));
         }
         if (!ok) break;
         // ---- item end: combine the two warps' (max used, sum, true max) ----
@@ -586,14 +634,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         if (it >= 2 && !(ok = wait_warp(bar(kFinFree0 + fb), ((it >> 1) - 1) & 1u, abort_flag, true))) break;
         st_async_b32x2(r_fin0 + fb * kFinBytes + (uint32_t)row * 8u, r_finbar0 + 8u * fb, f2u(l), f2u(f));
       }
-      // Drain: the value CTA's last P-slot credits and (l, f) acknowledgements
-      // arrive here; wait for them before the CTA can exit. Each warp waits
-      // for the credits of its own tiles among the last kPSlots.
-      for (uint32_t k = 0; ok && k < (uint32_t)kPSlots && k < g; ++k) {
-        const uint32_t gl = g - 1 - k;
-        if ((gl & 1u) != e) continue;
-        ok = wait_warp(bar(kPSlotFree0 + gl % kPSlots), (gl / kPSlots) & 1u, abort_flag);
-      }
+      // Drain: the value CTA's last (l, f) acknowledgements arrive here; wait
+      // for them before the CTA can exit (the sender waits for the P-slot
+      // credits).
       if (ok && e == 0) {
         for (uint32_t k = 0; ok && k < 2u && k < it; ++k) {
           const uint32_t il = it - 1 - k;

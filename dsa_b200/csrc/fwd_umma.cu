@@ -169,30 +169,6 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
-// Bounded wait (lane 0 polls) until a shared word equals `value`; the same
-// result in every lane.
-__device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t value, volatile int* abort) {
-  bool ok = true;
-  if ((threadIdx.x & 31) == 0 && *word != value) {
-    const unsigned long long start = global_ns();
-    for (uint32_t k = 1; *word != value; ++k) {
-      if ((k & 15u) == 0) {
-        if (*abort) {
-          ok = false;
-          break;
-        }
-        if (global_ns() - start > kWaitLimitNs) {
-          *abort = 1;
-          ok = false;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-  }
-  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-}
-
 // Columns [cb0, cb1) (multiples of 32) of O for this thread's head row (TMEM
 // lane `o_lane`) -> the output (O / l as BF16, split 1) or the FP32 partial
 // (O * f); two 32-column chunks in flight so each load overlaps a store.

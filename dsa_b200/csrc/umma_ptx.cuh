@@ -95,6 +95,30 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Bounded wait (lane 0 polls) until a shared word equals `value`; the same
+// result in every lane of the warp.
+__device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t value, volatile int* abort) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0 && *word != value) {
+    const unsigned long long start = global_ns();
+    for (uint32_t k = 1; *word != value; ++k) {
+      if ((k & 15u) == 0) {
+        if (*abort) {
+          ok = false;
+          break;
+        }
+        if (global_ns() - start > kWaitLimitNs) {
+          *abort = 1;
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 // ---- cluster / DSMEM ------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -130,6 +154,23 @@ __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint32_t remot
           remote_addr),
       "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar)
       : "memory");
+}
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into a peer CTA's (shared::cluster address
+// from mapa); complete_tx on the peer's mbarrier `remote_bar`. No multicast.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t remote_dst, uint32_t local_src, uint32_t bytes,
+                                                  uint32_t remote_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          remote_dst),
+      "r"(local_src), "r"(bytes), "r"(remote_bar)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's bulk copy groups still read their source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
