@@ -134,6 +134,14 @@ constexpr uint32_t kOffTmemSlot = kOffBar + kBarCount * 8u;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 8u;
 constexpr uint32_t kOffReq = kOffAbort + 8u;
 constexpr uint32_t kOffStageTile = kOffReq + 8u;        // score CTA: tile each stage is being filled with
+// score CTA: validity bits of tile g's 32 keys at entry g % 16, tagged with
+// g, written by the tile's gather warp. A gather warp can be at most 13
+// tiles ahead of the softmax warp reading the entry (stage reuse waits for
+// the QK of tile g - 5, which waits for the softmax of tile g - 11 to read
+// its S, which that warp does after finishing tile g - 13 or after the
+// running max of tile g - 14, posted after its entry was read).
+constexpr int kMaskRing = 16;
+constexpr uint32_t kOffMaskRing = kOffStageTile + 4u * kKStages + 4u;  // [16] {bits, tag}, 8-byte aligned
 constexpr uint32_t kOffData = 1024u;
 constexpr uint32_t kOffK = kOffData;                     // score CTA stages
 constexpr uint32_t kOffV = kOffData;                     // value CTA stages
@@ -154,7 +162,7 @@ constexpr uint32_t kTmemQ = 0;      // score CTA: Q, 288 columns (dims 0..575 as
 constexpr uint32_t kTmemS = 288;    // score CTA: S buffers, 32 columns each
 constexpr uint32_t kTmemO = 0;      // value CTA: O, 512 columns
 
-static_assert(kOffStageTile + 4u * kKStages <= kOffData, "barrier block");
+static_assert(kOffMaskRing % 8 == 0 && kOffMaskRing + 8u * kMaskRing <= kOffData, "barrier block");
 static_assert(kLSlots % 2 == 0, "a staging slot must always belong to the same softmax warp");
 static_assert(kOffLocal % 1024 == 0 && kMsgBytes % 16 == 0, "bulk copy alignment");
 static_assert(kOffSlot % 1024 == 0 && kSlotBytes % 1024 == 0, "P slots are 1024-aligned");
@@ -225,6 +233,13 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
+// 8-byte shared-memory store / load (both words together)
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void ld_shared_v2(uint32_t addr, uint32_t& a, uint32_t& b) {
+  asm volatile("ld.volatile.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr) : "memory");
+}
 __device__ __forceinline__ void st_async_b32x2(uint32_t remote_addr, uint32_t remote_bar, uint32_t a, uint32_t b) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(
                    remote_addr),
@@ -317,6 +332,8 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       }
       for (int s = 0; s < kKStages; ++s)
         reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = 0xffffffffu;
+      for (int k = 0; k < kMaskRing; ++k)
+        reinterpret_cast<volatile uint32_t*>(sbase + kOffMaskRing)[2 * k + 1] = 0xffffffffu;
     } else {
       for (int s = 0; s < kVStages; ++s) {
         mbar_init(bar(kVFull0 + s), 1);
@@ -367,7 +384,13 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       while (cur.item < n_items) {
         if (n > 0 && !(ok = wait_warp(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag))) break;
         // the stage's previous tile (g - 5) is consumed, so its Full phase completed
-        if (lane == 0) reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = s + kKStages * n;
+        const uint32_t gt = s + kKStages * n;  // the tile this warp fills
+        const uint32_t vbits = __ballot_sync(0xffffffffu, (idx_cur >= 0) & (idx_cur < L));
+        if (lane == 0) {
+          reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = gt;
+          // validity bits of the tile for the softmax (one 8-byte store: bits and tag together)
+          st_shared_v2(base + kOffMaskRing + 8u * (gt % kMaskRing), vbits, gt);
+        }
         const int row = min(max(idx_cur, 0), L - 1);  // clamped address; masked by the softmax
         gather_rows(stage, p.kv + (size_t)cur.w.batch * L * kDimLatent,
                     p.k_rope + (size_t)cur.w.batch * L * kDimRope, row, lane, true);
@@ -483,10 +506,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       // P row offset in a slot (SW64 K-major: 8-row groups of 512 B, 16-byte chunks swizzled)
       const uint32_t prow = (uint32_t)(row >> 3) * 512u + (uint32_t)(row & 7) * 64u;
       uint32_t xn = 0;  // item-end exchanges done with the other warp of this quadrant
-      // This warp's tiles: e, e + 2, ... of the cluster's tile sequence; the
-      // indices of the next one are loaded one tile ahead (validity mask).
-      PCursor nxt = pcursor_start(p, n_items, cid, ncl, (int)e);
-      int idx_nxt = pcursor_index(p, nxt, n_items, lane);
+      // This warp's tiles: e, e + 2, ... of the cluster's tile sequence.
       uint32_t g = 0, it = 0;
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
@@ -520,11 +540,26 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
               prefetch_l2_bulk(p.q_rope + qn * kDimRope, 16384u);
           }
           const uint32_t i = g % kSBufs;
-          const int idx = idx_nxt;  // this tile's indices (loaded one tile ahead)
-          pcursor_advance(p, n_items, ncl, nxt, 2);
-          idx_nxt = pcursor_index(p, nxt, n_items, lane);
-          const uint32_t mbits = __ballot_sync(0xffffffffu, (idx >= 0) & (idx < L));
-          if (!(ok = wait_warp(bar(kSFull0 + i), (g / kSBufs) & 1u, abort_flag))) break;
+          // S complete (a non-blocking test first: it almost always is)
+          {
+            const bool rdy = lane == 0 ? mbar_test(bar(kSFull0 + i), (g / kSBufs) & 1u) : false;
+            if (__shfl_sync(0xffffffffu, rdy ? 1 : 0, 0) == 0 &&
+                !(ok = wait_warp(bar(kSFull0 + i), (g / kSBufs) & 1u, abort_flag)))
+              break;
+          }
+          // validity bits of the tile's keys, published by its gather warp
+          // (written before the gather, so present once S is)
+          uint32_t mbits, mtag;
+          {
+            const uint32_t ent = base + kOffMaskRing + 8u * (g % kMaskRing);
+            ld_shared_v2(ent, mbits, mtag);
+            if (mtag != g) {
+              if (!(ok = wait_word_warp(reinterpret_cast<volatile uint32_t*>(sbase + kOffMaskRing + 8u * (g % kMaskRing) + 4u),
+                                        g, abort_flag)))
+                break;
+              ld_shared_v2(ent, mbits, mtag);
+            }
+          }
           tc_fence_after();
           float x[32];
           {
