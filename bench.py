@@ -411,11 +411,13 @@ def main():
     # share the link in opposite directions), with two buffer sets; the value
     # is the steady-state time per step.
     e2e_steps = args.e2e_steps or max(1, min(args.steps, 5))
-    host_in = [t.cpu().pin_memory() for t in data]
+    # this rank's inputs: its query rows of q, q_rope and the indices, and
+    # kv / k_rope of the batch rows those queries read
+    host_in = [[t.cpu().pin_memory() for t in vw] for vw in views]
     n_buf = 2
-    dev_in = [[torch.empty_like(t) for t in data] for _ in range(n_buf)]
+    dev_in = [[[torch.empty_like(t, device=device) for t in hp] for hp in host_in] for _ in range(n_buf)]
     out_host = [None] * n_buf
-    h2d_bytes = sum(t.numel() * t.element_size() for t in host_in)
+    h2d_bytes = sum(t.numel() * t.element_size() for hp in host_in for t in hp)
     data = None
     views = None
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
@@ -429,14 +431,12 @@ def main():
         step_no[0] += 1
         s_in.wait_event(ev_fwd[b])  # the forward that last read these inputs is done
         with torch.cuda.stream(s_in):
-            for hsrc, ddst in zip(host_in, dev_in[b]):
-                ddst.copy_(hsrc, non_blocking=True)
+            for hp, dp in zip(host_in, dev_in[b]):
+                for hsrc, ddst in zip(hp, dp):
+                    ddst.copy_(hsrc, non_blocking=True)
             ev_in[b].record(s_in)
         stream.wait_event(ev_in[b])
-        d = dev_in[b]
-        vws = [(d[0][b0:b1, s0:s1], d[1][b0:b1], d[2][b0:b1, s0:s1], d[3][b0:b1], d[4][b0:b1, s0:s1])
-               for b0, b1, s0, s1 in pieces]
-        outs = [dsa_b200.forward(*v, config=tuning) for v in vws]
+        outs = [dsa_b200.forward(*dp, config=tuning) for dp in dev_in[b]]
         ev_fwd[b].record(stream)
         if out_host[b] is None:
             out_host[b] = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in o] for o in outs]
