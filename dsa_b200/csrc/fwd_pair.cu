@@ -78,7 +78,6 @@ constexpr int kLSlots = 4;      // score CTA: local P staging slots (even: slot 
 constexpr int kSendWarp = kKStages;  // score CTA: warp 5 sends the staged P
 constexpr int kSBufs = 6;       // score CTA: S accumulators in TMEM
 constexpr int kQkIssuers = 6;   // score CTA: QK issuer i takes tiles g = i mod 6
-constexpr int kQkQHelpers = 4;  // issuers 0-3 also load Q chunks of their lane quadrant
 constexpr int kVStages = 5;     // value CTA: gathered value rows
 constexpr int kPSlots = 6;      // value CTA: P slots
 constexpr int kPrThreads = 640;
@@ -111,6 +110,7 @@ enum Bar {
   kEmpty0 = kFull0 + kKStages,      // QK commit (the softmax takes validity from the indices)
   kQFull = kEmpty0 + kKStages,
   kQSeen,
+  kQkDone,                          // every QK MMA of the item is done (one commit per issuer)
   kSFull0,
   kSFree0 = kSFull0 + kSBufs,
   kFinFree0 = kSFree0 + kSBufs,     // 2: value CTA has read the (l, f) buffer
@@ -292,6 +292,53 @@ __device__ __forceinline__ void load_q_chunk(const FwdParams& p, size_t qrow, in
   tmem_st32(taddr, r);
 }
 
+// Chunks [c0, c1) of one Q head row, two chunks' loads in flight at a time
+// (`tq` = this lane's TMEM address of chunk 0).
+__device__ __forceinline__ void load_q_chunks(const FwdParams& p, size_t qrow, int c0, int c1, uint32_t tq) {
+#pragma unroll 1
+  for (int ch = c0; ch < c1; ch += 2) {
+    if (ch + 1 == c1) {
+      load_q_chunk(p, qrow, ch, tq + (uint32_t)ch * 32u);
+      break;
+    }
+    uint32_t r[64];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int cc = ch + h;
+      const uint4* s4 = cc < 8 ? reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent) + cc * 8
+                               : reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint4 v = __ldg(s4 + k);
+        r[32 * h + 4 * k] = v.x;
+        r[32 * h + 4 * k + 1] = v.y;
+        r[32 * h + 4 * k + 2] = v.z;
+        r[32 * h + 4 * k + 3] = v.w;
+      }
+    }
+    tmem_st32(tq + (uint32_t)ch * 32u, r);
+    tmem_st32(tq + (uint32_t)(ch + 1) * 32u, r + 32);
+  }
+}
+
+// Q chunks that QK issuer i (warp kQkWarp0 + i, TMEM lane quadrant
+// (kQkWarp0 + i) % 4) loads for each item: chunks 2..8 of its quadrant, split
+// between the two issuers of quadrants 2 and 3; the quadrant's two softmax
+// warps load chunks 0 and 1.
+__device__ __forceinline__ void issuer_q_chunks(int i, int* c0, int* c1) {
+  const int quad = (kQkWarp0 + i) & 3;
+  if (quad < 2) {  // the only issuer of its quadrant
+    *c0 = 2;
+    *c1 = 9;
+  } else if (i < 4) {
+    *c0 = 2;
+    *c1 = 6;
+  } else {
+    *c0 = 6;
+    *c1 = 9;
+  }
+}
+
 __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -313,8 +360,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         mbar_init(bar(kFull0 + s), 1);
         mbar_init(bar(kEmpty0 + s), 1);
       }
-      mbar_init(bar(kQFull), kSoftWarps + kQkQHelpers);  // Q chunks: 8 softmax warps + 4 QK issuers
+      mbar_init(bar(kQFull), kSoftWarps + kQkIssuers);  // Q chunks: 8 softmax warps + 6 QK issuers
       mbar_init(bar(kQSeen), kQkIssuers);
+      mbar_init(bar(kQkDone), kQkIssuers);
       for (int i = 0; i < kSBufs; ++i) {
         mbar_init(bar(kSFull0 + i), 1);
         mbar_init(bar(kSFree0 + i), 4);
@@ -416,14 +464,12 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
-        // Issuers 0-3: Q chunks 2, 5, 8 of their lane quadrant's head rows.
-        // Both softmax warps of the quadrant finished the previous item (its
-        // item-end exchange), so every QK MMA of that item has completed.
-        if (i < (uint32_t)kQkQHelpers) {
-          if (it > 0 && !(ok = wait_warp(bar(kXchg0 + quad), (it - 1) & 1u, abort_flag))) break;
-          const size_t qrow = (size_t)w.token * kPrHeads + quad * 32 + lane;
-#pragma unroll 1
-          for (int ch = 2; ch < 9; ch += 3) load_q_chunk(p, qrow, ch, tmem + t_lane + kTmemQ + ch * 32);
+        // This issuer's Q chunks of its lane quadrant's head rows: for the
+        // first item here, for later items at the end of the previous one.
+        int qc0, qc1;
+        issuer_q_chunks((int)i, &qc0, &qc1);
+        if (it == 0) {
+          load_q_chunks(p, (size_t)w.token * kPrHeads + quad * 32 + lane, qc0, qc1, tmem + t_lane + kTmemQ);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
@@ -460,6 +506,22 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             mma_commit(bar(kEmpty0 + s));
           }
           __syncwarp();
+        }
+        if (!ok) break;
+        // Once every issuer's QK MMAs of this item are done, the Q columns are
+        // free: load this issuer's chunks of the next item's Q while the
+        // softmax warps finish this item.
+        if (elect_one()) mma_commit(bar(kQkDone));
+        __syncwarp();
+        if (item + ncl < n_items) {
+          if (!(ok = wait_warp(bar(kQkDone), it & 1u, abort_flag))) break;
+          tc_fence_after();
+          const PItem wn = make_pitem(p, item + ncl);
+          load_q_chunks(p, (size_t)wn.token * kPrHeads + quad * 32 + lane, qc0, qc1, tmem + t_lane + kTmemQ);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kQFull));
         }
       }
     } else if (warp == kSendWarp) {
@@ -510,15 +572,14 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       uint32_t g = 0, it = 0;
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
-        // Q of this head row -> TMEM columns [0, 288): chunks e, e + 3, e + 6
-        // here, chunks 2, 5, 8 by the quadrant's QK issuer. The previous
-        // item's QK MMAs are complete (every S was waited for) and every
-        // issuer has seen the previous item's Q.
+        // Q of this head row -> TMEM columns [0, 288): chunk e here, chunks
+        // 2..8 by the quadrant's QK issuers (loaded during the previous item's
+        // last tiles). The previous item's QK MMAs are complete (every S was
+        // waited for) and every issuer has seen the previous item's Q.
         if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag))) break;
         {
           const size_t qrow = (size_t)w.token * kPrHeads + row;
-#pragma unroll 1
-          for (int ch = (int)e; ch < 9; ch += 3) load_q_chunk(p, qrow, ch, tmem + t_lane + kTmemQ + ch * 32);
+          load_q_chunk(p, qrow, (int)e, tmem + t_lane + kTmemQ + e * 32u);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
