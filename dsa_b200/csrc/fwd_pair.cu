@@ -109,7 +109,6 @@ enum Bar {
   kFull0 = 0,
   kEmpty0 = kFull0 + kKStages,      // QK commit (the softmax takes validity from the indices)
   kQFull = kEmpty0 + kKStages,
-  kQSeen,
   kQkDone,                          // every QK MMA of the item is done (one commit per issuer)
   kSFull0,
   kSFree0 = kSFull0 + kSBufs,
@@ -322,19 +321,18 @@ __device__ __forceinline__ void load_q_chunks(const FwdParams& p, size_t qrow, i
 }
 
 // Q chunks that QK issuer i (warp kQkWarp0 + i, TMEM lane quadrant
-// (kQkWarp0 + i) % 4) loads for each item: chunks 2..8 of its quadrant, split
-// between the two issuers of quadrants 2 and 3; the quadrant's two softmax
-// warps load chunks 0 and 1.
+// (kQkWarp0 + i) % 4) loads for each item: all nine chunks of its quadrant's
+// head rows, split between the two issuers of quadrants 2 and 3.
 __device__ __forceinline__ void issuer_q_chunks(int i, int* c0, int* c1) {
   const int quad = (kQkWarp0 + i) & 3;
   if (quad < 2) {  // the only issuer of its quadrant
-    *c0 = 2;
+    *c0 = 0;
     *c1 = 9;
   } else if (i < 4) {
-    *c0 = 2;
-    *c1 = 6;
+    *c0 = 0;
+    *c1 = 5;
   } else {
-    *c0 = 6;
+    *c0 = 5;
     *c1 = 9;
   }
 }
@@ -360,8 +358,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         mbar_init(bar(kFull0 + s), 1);
         mbar_init(bar(kEmpty0 + s), 1);
       }
-      mbar_init(bar(kQFull), kSoftWarps + kQkIssuers);  // Q chunks: 8 softmax warps + 6 QK issuers
-      mbar_init(bar(kQSeen), kQkIssuers);
+      mbar_init(bar(kQFull), kQkIssuers);  // Q chunks: the 6 QK issuers
       mbar_init(bar(kQkDone), kQkIssuers);
       for (int i = 0; i < kSBufs; ++i) {
         mbar_init(bar(kSFull0 + i), 1);
@@ -475,11 +472,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(kQFull));
         }
-        // Every issuer observes every item's Q and acknowledges it, so none
-        // can fall a barrier phase behind.
+        // Every issuer waits for every item's Q (all chunks of all quadrants),
+        // so none can fall a barrier phase behind.
         if (!(ok = wait_warp(bar(kQFull), it & 1u, abort_flag))) break;
-        if (elect_one()) mbar_arrive(bar(kQSeen));
-        __syncwarp();
         for (int t = 0; t < w.ntiles; ++t, ++g) {
           if (g % kQkIssuers != i) continue;
           const uint32_t s = g % kKStages, b = g % kSBufs;
@@ -572,19 +567,8 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       uint32_t g = 0, it = 0;
       for (int item = cid; item < n_items && ok; item += ncl, ++it) {
         const PItem w = make_pitem(p, item);
-        // Q of this head row -> TMEM columns [0, 288): chunk e here, chunks
-        // 2..8 by the quadrant's QK issuers (loaded during the previous item's
-        // last tiles). The previous item's QK MMAs are complete (every S was
-        // waited for) and every issuer has seen the previous item's Q.
-        if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag))) break;
-        {
-          const size_t qrow = (size_t)w.token * kPrHeads + row;
-          load_q_chunk(p, qrow, (int)e, tmem + t_lane + kTmemQ + e * 32u);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(kQFull));
-        }
+        // (Q of the item is loaded into TMEM by the QK issuers, during the
+        // previous item's last tiles.)
         // this warp's running state for the item
         float m_w = kNegFltMax;     // max used for this warp's latest tile
         float m_true = kNegFltMax;  // true max over this warp's tiles
