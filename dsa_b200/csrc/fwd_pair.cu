@@ -43,15 +43,15 @@
 //              per tile) right after its row-max reduction, and the other warp
 //              waits for it before deciding its own, so the exponentials and
 //              the P transfer of consecutive tiles overlap. Key validity comes
-//              from the indices (loaded a tile ahead), so a stage is free as
-//              soon as its QK MMAs complete. 14-19 QK issuers (tile g ->
-//              issuer g % 6: issuing a tcgen05.mma occupies the issuing warp's
-//              scheduler, so the 36 MMAs of each tile are spread over the
-//              schedulers) into S buffer g % 6 (a buffer returns to the
-//              issuers only after its softmax read). At an
-//              item boundary the issuers also load three of the nine Q chunks
-//              of their lane quadrant, and the next item's Q is prefetched
-//              into L2 eight tiles ahead.
+//              from the gather warps (a tagged ring of per-tile bit masks), so
+//              a stage is free as soon as its QK MMAs complete. 14-19 QK
+//              issuers (tile g -> issuer g % 6: issuing a tcgen05.mma occupies
+//              the issuing warp's scheduler, so the 36 MMAs of each tile are
+//              spread over the schedulers) into S buffer g % 6 (a buffer
+//              returns to the issuers only after its softmax read). The
+//              issuers also load Q into TMEM: once every QK MMA of an item is
+//              done, all nine chunks of the next item's Q (prefetched into L2
+//              eight tiles ahead), while the softmax warps finish the item.
 //   value CTA: 0-4 gather of the 512 latent dims (warp w owns stage w), 6 PV
 //              issuer, 8-19 rescale and epilogue (three warps per lane
 //              quadrant, O * (1/l) -> output with 32-byte stores).
