@@ -523,7 +523,7 @@ def main():
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        dev_data = [t.to(device, non_blocking=True) for t in host_in]
+        dev_data = [t.to(device, non_blocking=True) for t in host_in[0]]  # one GPU: one piece, all queries
         torch.cuda.synchronize()
         sec, rows, threads = cpu_reference_rate(dev_data, shape, budget_s=args.cpu_budget)
         line["cpu_baseline"] = {"value": sec * 1e6, "unit": "us/call", "cores": threads, "kind": "port",
