@@ -1,4 +1,4 @@
-// Inline-PTX wrappers for the sm_100a tcgen05 / TMA / cluster path.
+// Inline-PTX wrappers for the sm_100a tcgen05 / bulk-copy / cluster path.
 //
 // Every spin on an mbarrier is bounded (kWaitLimitNs of wall time read from
 // %globaltimer); a wait that gives up returns false and the caller reports
@@ -125,35 +125,10 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %cluster_ctarank;" : "=r"(r));
   return r;
 }
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %nclusterid.x;" : "=r"(r));
-  return r;
-}
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
-               : "memory");
-}
-// Asynchronous 16-byte store into a peer CTA's shared memory that signals
-// complete_tx on the peer's mbarrier when the bytes have landed.
-__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint32_t remote_bar, float a, float b,
-                                            float c, float d) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-          remote_addr),
-      "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar)
-      : "memory");
 }
 // Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
 // from this CTA's shared memory into a peer CTA's (shared::cluster address
@@ -205,29 +180,6 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
-// ---- TMA --------------------------------------------------------------------------
-__device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
-}
-// 2-D tiled load of one box into this CTA's shared memory.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* desc, uint32_t bar, int32_t c0,
-                                            int32_t c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(c0), "r"(c1)
-      : "memory");
-}
-// Four rows (row0..row3) of one box-wide column block into this CTA's
-// shared memory (box height 1 in the tensor map).
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* desc, uint32_t bar, int32_t col,
-                                            int32_t r0, int32_t r1, int32_t r2, int32_t r3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-      : "memory");
-}
 
 // ---- tcgen05 -------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
