@@ -783,7 +783,6 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           if (t == 0 && it > 0 && !(ok = wait_warp(bar(kOFree), (it - 1) & 1u, abort_flag))) break;
           const uint32_t vstage = base + kOffV + vs * kVStage;
           if (elect_one()) {
-            fence_proxy_async_smem();  // P arrived through st.async
             tc_fence_after();
 #pragma unroll
             for (int j = 0; j < kPrBN / 16; ++j) {
