@@ -27,6 +27,7 @@ FAMILY_UMMA = 2
 FAMILY_UMMA_PAIR = 3
 FAMILY_STREAM = 4
 FAMILY_KEYS = 5
+FAMILY_PAIR_UNION = 6
 
 # Every entry point declared in include/dsa_b200.h.
 EXPORTS = (

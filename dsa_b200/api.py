@@ -25,7 +25,7 @@ LaunchRecord = namedtuple("LaunchRecord", "name family heads_per_cta keys_per_ti
 
 _FAMILY_NAMES = {_native.FAMILY_WARP_MMA: "warp_mma", _native.FAMILY_UMMA: "umma",
                  _native.FAMILY_UMMA_PAIR: "umma_pair", _native.FAMILY_STREAM: "stream",
-                 _native.FAMILY_KEYS: "keys"}
+                 _native.FAMILY_KEYS: "keys", _native.FAMILY_PAIR_UNION: "pair_union"}
 
 
 def _check_inputs(q, kv, q_rope, k_rope, indices):
@@ -95,6 +95,8 @@ def _launch_from_tuning(config, shape):
     if config.bm == 128:
         family = _native.FAMILY_UMMA_PAIR if config.pv_cols == 512 else _native.FAMILY_UMMA
         launch = _native.Launch(family, 128, config.bn, config.split)
+    elif config.bn == 32 and config.pv_cols == 128:
+        launch = _native.Launch(_native.FAMILY_PAIR_UNION, 128, config.bn, config.split)
     elif config.bn == 32:
         launch = _native.Launch(_native.FAMILY_STREAM, 16, config.bn, config.split)
     elif config.pv_cols == 128:

@@ -20,7 +20,10 @@ B200:
   family (two CTAs per query, each over half of the 512 columns). For
   ``bm < 128, bn == 64``, 128 selects the keys family (tcgen05 with the
   selected keys as the MMA's M dimension and the value product computed in
-  128-column blocks) instead of the warp-MMA family.
+  128-column blocks) instead of the warp-MMA family; for ``bm < 128,
+  bn == 32``, 128 selects the union launch of the pair family (blocks of
+  128 / H queries over the union of their selected keys, H in {16, 32, 64})
+  instead of the stream family.
 * ``direct_nz``, ``share_score`` — Ascend data-movement knobs (NZ packing,
   score/PV UB sharing) with no counterpart on sm_100a. They are type-checked
   as in the reference but do not change the launch.

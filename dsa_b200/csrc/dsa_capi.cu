@@ -51,6 +51,22 @@ Layout partial_layout(int64_t tokens, int64_t heads, int64_t split) {
   return lay;
 }
 
+// Union launch: per block of 128 / H queries, up to (128 / H) * topk union
+// entries and their count.
+struct UnionLayout {
+  uint64_t ent_off, len_off, total;
+  int64_t blocks, ucap;
+};
+UnionLayout union_layout(int64_t tokens, int64_t heads, int64_t topk) {
+  UnionLayout u{0, 0, 0, 0, 0};
+  const int64_t qpb = 128 / heads;
+  u.blocks = tokens / qpb;
+  u.ucap = qpb * topk;
+  u.len_off = align_up((uint64_t)u.blocks * (uint64_t)u.ucap * sizeof(int32_t));
+  u.total = u.len_off + align_up((uint64_t)u.blocks * sizeof(int32_t));
+  return u;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -90,6 +106,12 @@ int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t leng
     }
     case DSA_FAMILY_KEYS: {
       if (launch->heads_per_cta != 16 || heads % 16 != 0 || bn != 64) return DSA_STATUS_UNSUPPORTED;
+      break;
+    }
+    case DSA_FAMILY_PAIR_UNION: {
+      if (launch->heads_per_cta != 128 || bn != 32 || launch->split != 1) return DSA_STATUS_UNSUPPORTED;
+      if (heads != 16 && heads != 32 && heads != 64) return DSA_STATUS_UNSUPPORTED;
+      if (queries % (128 / heads) != 0 || length >= (1 << 24)) return DSA_STATUS_UNSUPPORTED;
       break;
     }
     case DSA_FAMILY_UMMA:
@@ -140,6 +162,22 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
     *out = e;
     return DSA_STATUS_OK;
   }
+  // union launch of the pair family for 16 heads: blocks of 8 queries of one
+  // batch row over the union of their keys, when the blocks fill the
+  // clusters and the keys are dense enough (L <= 4 TOPK: the union of 8
+  // queries' keys is then at most ~3.6 TOPK, against 8 TOPK key-rows for the
+  // per-query form)
+  if (heads == 16 && queries % 8 == 0 && length <= 4 * topk && length < (1 << 24)) {
+    const int pair_ctas = dsa::pair_max_ctas();
+    if (pair_ctas > 0 && batch * queries / 8 >= pair_ctas / 2) {
+      e.family = DSA_FAMILY_PAIR_UNION;
+      e.heads_per_cta = 128;
+      e.keys_per_tile = 32;
+      e.split = 1;
+      *out = e;
+      return DSA_STATUS_OK;
+    }
+  }
   // stream family: persistent CTAs over (token, 16-head group, split)
   // items; split the TOPK range only until every resident CTA has an item.
   e.family = DSA_FAMILY_STREAM;
@@ -165,6 +203,7 @@ uint64_t dsa_fwd_workspace_bytes(const dsa_fwd_args_t* a) {
     return 0;
   if (dsa_check_launch(a->batch, a->queries, a->heads, a->length, a->topk, &e) != DSA_STATUS_OK)
     return 0;
+  if (e.family == DSA_FAMILY_PAIR_UNION) return union_layout(a->batch * a->queries, a->heads, a->topk).total;
   return partial_layout(a->batch * a->queries, a->heads, e.split).total;
 }
 
@@ -187,6 +226,12 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
 
   const int64_t tokens = a->batch * a->queries;
   const Layout lay = partial_layout(tokens, a->heads, e.split);
+  if (e.family == DSA_FAMILY_PAIR_UNION) {
+    const UnionLayout ul = union_layout(tokens, a->heads, a->topk);
+    if (a->workspace == nullptr || a->workspace_bytes < ul.total ||
+        (reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0)
+      return DSA_STATUS_WORKSPACE_TOO_SMALL;
+  }
   if (lay.total > 0) {
     if (a->workspace == nullptr || a->workspace_bytes < lay.total ||
         (reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0)
@@ -229,10 +274,30 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
     case DSA_FAMILY_UMMA_PAIR: err = dsa::launch_fwd_pair(p, s); break;
     case DSA_FAMILY_STREAM: err = dsa::launch_fwd_stream(p, s); break;
     case DSA_FAMILY_KEYS: err = dsa::launch_fwd_keys(p, s); break;
+    case DSA_FAMILY_PAIR_UNION: {
+      // blocks of 128 / H queries become 128-row items over their union entries
+      const UnionLayout ul = union_layout(tokens, a->heads, a->topk);
+      const int qpb = 128 / (int)a->heads;
+      int32_t* uent = reinterpret_cast<int32_t*>(ws + ul.ent_off);
+      int32_t* ulen = reinterpret_cast<int32_t*>(ws + ul.len_off);
+      err = dsa::launch_union_build(p.ids, p.topk, p.length, qpb, (int)ul.blocks, uent, ulen, (int)ul.ucap, s);
+      if (err != cudaSuccess) break;
+      dsa::FwdParams pu = p;
+      pu.tokens = (int)ul.blocks;
+      pu.queries = (int)(a->queries / qpb);
+      pu.heads = 128;
+      pu.heads_per_cta = 128;
+      pu.uent = uent;
+      pu.ulen = ulen;
+      pu.ucap = (int)ul.ucap;
+      pu.u_row_shift = a->heads == 16 ? 4 : a->heads == 32 ? 5 : 6;
+      err = dsa::launch_fwd_pair_union(pu, s);
+      break;
+    }
     default: return DSA_STATUS_UNSUPPORTED;
   }
   if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;
-  int launches = 1;
+  int launches = e.family == DSA_FAMILY_PAIR_UNION ? 2 : 1;  // union build + pair kernel
   if (e.split > 1) {
     err = dsa::launch_merge(p.part_num, p.part_max, p.part_sum, p.out, p.out_max, p.out_sum,
                             p.tokens, p.heads, p.split, s);

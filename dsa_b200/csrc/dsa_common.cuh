@@ -38,6 +38,13 @@ struct FwdParams {
   float* part_num;        // split > 1: [T, S, H, 512]
   float* part_max;        // split > 1: [T, S, H]
   float* part_sum;        // split > 1: [T, S, H]
+  // Union launch of the pair family (heads = 128 rows of 128 / H queries):
+  // per block, `ulen` entries of key | (query membership << 24) at
+  // uent[block * ucap ...]; row r of a block belongs to query r >> u_row_shift.
+  const int32_t* uent;
+  const int32_t* ulen;
+  int ucap;
+  int u_row_shift;
   int32_t* status;
   int batch, queries, heads, length, topk;
   int tokens;             // batch * queries
@@ -150,6 +157,9 @@ cudaError_t launch_fwd_pair(const FwdParams& p, cudaStream_t stream);
 int pair_max_ctas();
 cudaError_t launch_fwd_stream(const FwdParams& p, cudaStream_t stream);
 cudaError_t launch_fwd_keys(const FwdParams& p, cudaStream_t stream);
+cudaError_t launch_fwd_pair_union(const FwdParams& p, cudaStream_t stream);
+cudaError_t launch_union_build(const int32_t* ids, int topk, int length, int qpb, int blocks, int32_t* uent,
+                               int32_t* ulen, int ucap, cudaStream_t stream);
 // CTAs of the stream family resident at once (-1 on error).
 int stream_max_ctas();
 int keys_max_ctas();

@@ -149,7 +149,11 @@ constexpr uint32_t kOffFin = kOffSlot + kPSlots * kSlotBytes;
 constexpr uint32_t kOffLocal = kOffK + kKStages * kKStage;  // score CTA: P staging slots
 constexpr uint32_t kOffX = kOffLocal + kLSlots * kSlotBytes;  // score CTA: [2][4 quads][2 warps][3][32] floats
 constexpr uint32_t kOffM = kOffX + 2u * 4u * 2u * 3u * 32u * 4u;  // score CTA: [2][4 quads][32] running maxima
-constexpr uint32_t kSmemScore = kOffM + 2u * 4u * 32u * 4u;
+// score CTA, union launch: per tile one validity mask per query of the block
+// (8 words) and the tile tag (word 8), 48-byte entries, same ring indexing
+constexpr uint32_t kOffURing = kOffM + 2u * 4u * 32u * 4u;
+constexpr uint32_t kURingStride = 48u;
+constexpr uint32_t kSmemScore = kOffURing + kMaskRing * kURingStride;
 constexpr uint32_t kSmemValue = kOffFin + 2u * kFinBytes;
 constexpr uint32_t kSmemUsed = kSmemScore > kSmemValue ? kSmemScore : kSmemValue;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024u;  // slack for the 1024-byte alignment
@@ -162,6 +166,7 @@ constexpr uint32_t kTmemS = 288;    // score CTA: S buffers, 32 columns each
 constexpr uint32_t kTmemO = 0;      // value CTA: O, 512 columns
 
 static_assert(kOffMaskRing % 8 == 0 && kOffMaskRing + 8u * kMaskRing <= kOffData, "barrier block");
+static_assert(kOffURing % 16 == 0, "union ring entries are 16-byte aligned");
 static_assert(kLSlots % 2 == 0, "a staging slot must always belong to the same softmax warp");
 static_assert(kOffLocal % 1024 == 0 && kMsgBytes % 16 == 0, "bulk copy alignment");
 static_assert(kOffSlot % 1024 == 0 && kSlotBytes % 1024 == 0, "P slots are 1024-aligned");
@@ -177,7 +182,12 @@ __device__ __forceinline__ PItem make_pitem(const FwdParams& p, int item) {
   it.token = item / p.split;
   it.sp = item % p.split;
   it.batch = it.token / p.queries;
-  split_bounds(p.topk, kPrBN, p.split, it.sp, &it.kbeg, &it.kend);
+  if (p.uent != nullptr) {  // union launch: the block's union entries (split 1)
+    it.kbeg = 0;
+    it.kend = __ldg(p.ulen + it.token);
+  } else {
+    split_bounds(p.topk, kPrBN, p.split, it.sp, &it.kbeg, &it.kend);
+  }
   it.ntiles = (it.kend - it.kbeg + kPrBN - 1) / kPrBN;
   return it;
 }
@@ -207,11 +217,22 @@ __device__ __forceinline__ PCursor pcursor_start(const FwdParams& p, int n_items
   return c;
 }
 
-// Index of key `lane` of the cursor's tile (-1 past the split's end or past the last item).
+// Index of key `lane` of the cursor's tile (-1 past the split's end or past
+// the last item); for the union launch the packed entry key | bits << 24.
 __device__ __forceinline__ int pcursor_index(const FwdParams& p, const PCursor& c, int n_items, int lane) {
   if (c.item >= n_items) return -1;
   const int j = c.w.kbeg + c.t * kPrBN + lane;
-  return j < c.w.kend ? __ldg(p.ids + (size_t)c.w.token * p.topk + j) : -1;
+  if (j >= c.w.kend) return -1;
+  return p.uent != nullptr ? __ldg(p.uent + (size_t)c.w.token * p.ucap + j)
+                           : __ldg(p.ids + (size_t)c.w.token * p.topk + j);
+}
+// Row address of an index or union entry: clamped to [0, L - 1]; masked by
+// the softmax. A union entry is key | bits << 24 (negative when the block's
+// eighth query selected it); -1 marks a slot past the block's entries (no
+// key reaches 2^24 - 1).
+__device__ __forceinline__ int pcursor_row(const FwdParams& p, int idx, int L) {
+  if (p.uent != nullptr) return idx != -1 ? (idx & 0xFFFFFF) : 0;
+  return min(max(idx, 0), L - 1);
 }
 
 __device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(v); }
@@ -337,6 +358,9 @@ __device__ __forceinline__ void issuer_q_chunks(int i, int* c0, int* c1) {
   }
 }
 
+// kUnion: the union launch (keys from per-block union entries, one
+// validity mask per query of the block); otherwise one index row per item.
+template <bool kUnion>
 __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -379,6 +403,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = 0xffffffffu;
       for (int k = 0; k < kMaskRing; ++k)
         reinterpret_cast<volatile uint32_t*>(sbase + kOffMaskRing)[2 * k + 1] = 0xffffffffu;
+      if (kUnion)
+        for (int k = 0; k < kMaskRing; ++k)
+          reinterpret_cast<volatile uint32_t*>(sbase + kOffURing + k * kURingStride)[8] = 0xffffffffu;
     } else {
       for (int s = 0; s < kVStages; ++s) {
         mbar_init(bar(kVFull0 + s), 1);
@@ -430,13 +457,29 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         if (n > 0 && !(ok = wait_warp(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag))) break;
         // the stage's previous tile (g - 5) is consumed, so its Full phase completed
         const uint32_t gt = s + kKStages * n;  // the tile this warp fills
-        const uint32_t vbits = __ballot_sync(0xffffffffu, (idx_cur >= 0) & (idx_cur < L));
-        if (lane == 0) {
-          reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = gt;
-          // validity bits of the tile for the softmax (one 8-byte store: bits and tag together)
-          st_shared_v2(base + kOffMaskRing + 8u * (gt % kMaskRing), vbits, gt);
+        if constexpr (kUnion) {
+          // one mask per query of the block: entry lane selected by query j
+          uint32_t um[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            um[j] = __ballot_sync(0xffffffffu, idx_cur != -1 && (((uint32_t)idx_cur >> (24 + j)) & 1u));
+          if (lane == 0) {
+            reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = gt;
+            volatile uint32_t* ue = reinterpret_cast<volatile uint32_t*>(sbase + kOffURing + (gt % kMaskRing) * kURingStride);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ue[j] = um[j];
+            __threadfence_block();  // masks before the tag
+            ue[8] = gt;
+          }
+        } else {
+          const uint32_t vbits = __ballot_sync(0xffffffffu, (idx_cur >= 0) & (idx_cur < L));
+          if (lane == 0) {
+            reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = gt;
+            // validity bits of the tile for the softmax (one 8-byte store: bits and tag together)
+            st_shared_v2(base + kOffMaskRing + 8u * (gt % kMaskRing), vbits, gt);
+          }
         }
-        const int row = min(max(idx_cur, 0), L - 1);  // clamped address; masked by the softmax
+        const int row = pcursor_row(p, idx_cur, L);  // clamped address; masked by the softmax
         gather_rows(stage, p.kv + (size_t)cur.w.batch * L * kDimLatent,
                     p.k_rope + (size_t)cur.w.batch * L * kDimRope, row, lane, true);
         cp_async_commit();
@@ -595,7 +638,14 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           // validity bits of the tile's keys, published by its gather warp
           // (written before the gather, so present once S is)
           uint32_t mbits, mtag;
-          {
+          if constexpr (kUnion) {
+            // the mask of this row's query (row >> u_row_shift) in the block
+            const volatile uint32_t* ue =
+                reinterpret_cast<const volatile uint32_t*>(sbase + kOffURing + (g % kMaskRing) * kURingStride);
+            if (ue[8] != g && !(ok = wait_word_warp(const_cast<volatile uint32_t*>(ue + 8), g, abort_flag))) break;
+            __threadfence_block();  // the tag was written after the masks
+            mbits = ue[row >> p.u_row_shift];
+          } else {
             const uint32_t ent = base + kOffMaskRing + 8u * (g % kMaskRing);
             ld_shared_v2(ent, mbits, mtag);
             if (mtag != g) {
@@ -740,7 +790,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       uint32_t n = 0;
       while (cur.item < n_items) {
         if (n > 0 && !(ok = wait_warp(bar(kVFree0 + s), (n - 1) & 1u, abort_flag))) break;
-        const int row = min(max(idx_cur, 0), L - 1);  // invalid rows get P = 0
+        const int row = pcursor_row(p, idx_cur, L);  // invalid rows get P = 0
         gather_rows(stage, p.kv + (size_t)cur.w.batch * L * kDimLatent, nullptr, row, lane, false);
         cp_async_commit();
         const int idx_nx2 = pcursor_index(p, nx2, n_items, lane);
@@ -939,8 +989,10 @@ bool pair_launch_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, int 
 int pair_max_ctas() {
   static int cached = -1;
   if (cached > 0) return cached;
-  if (cudaFuncSetAttribute(fwd_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-      cudaSuccess)
+  if (cudaFuncSetAttribute(fwd_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(fwd_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
+          cudaSuccess)
     return -1;
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute attr;
@@ -950,13 +1002,14 @@ int pair_max_ctas() {
     return -1;
   pair_launch_config(&cfg, &attr, sms & ~1, nullptr);
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, fwd_pair_kernel, &cfg) != cudaSuccess || clusters <= 0) return -1;
+  if (cudaOccupancyMaxActiveClusters(&clusters, fwd_pair_kernel<false>, &cfg) != cudaSuccess || clusters <= 0)
+    return -1;
   cached = 2 * clusters;
   return cached;
 }
 
 cudaError_t launch_fwd_pair(const FwdParams& p, cudaStream_t stream) {
-  if (p.heads != kPrHeads || p.keys_per_tile != kPrBN) return cudaErrorInvalidValue;
+  if (p.heads != kPrHeads || p.keys_per_tile != kPrBN || p.uent != nullptr) return cudaErrorInvalidValue;
   const int max_ctas = pair_max_ctas();
   if (max_ctas <= 0) return cudaErrorInvalidConfiguration;
   const long long items = (long long)p.tokens * p.split;
@@ -964,7 +1017,23 @@ cudaError_t launch_fwd_pair(const FwdParams& p, cudaStream_t stream) {
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute attr;
   pair_launch_config(&cfg, &attr, (int)(2 * clusters), stream);
-  return cudaLaunchKernelEx(&cfg, fwd_pair_kernel, p);
+  return cudaLaunchKernelEx(&cfg, fwd_pair_kernel<false>, p);
+}
+
+// Union launch: p describes the blocks (tokens = blocks, heads = 128 rows,
+// queries = blocks per batch row, split 1) and their union entries.
+cudaError_t launch_fwd_pair_union(const FwdParams& p, cudaStream_t stream) {
+  if (p.heads != kPrHeads || p.keys_per_tile != kPrBN || p.uent == nullptr || p.ulen == nullptr ||
+      p.split != 1 || p.u_row_shift < 4 || p.u_row_shift > 6)
+    return cudaErrorInvalidValue;
+  const int max_ctas = pair_max_ctas();
+  if (max_ctas <= 0) return cudaErrorInvalidConfiguration;
+  const long long items = p.tokens;
+  const long long clusters = items < max_ctas / 2 ? items : max_ctas / 2;
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr;
+  pair_launch_config(&cfg, &attr, (int)(2 * clusters), stream);
+  return cudaLaunchKernelEx(&cfg, fwd_pair_kernel<true>, p);
 }
 
 }  // namespace dsa

@@ -76,9 +76,13 @@ typedef enum dsa_family {
                                computes scores + softmax, the other P.V over all 512 columns */
   DSA_FAMILY_STREAM = 4,    /* persistent warp-level MMA, 16 heads per CTA item, gather warps keep
                                the selected rows in flight; any H % 16 == 0, keys_per_tile 32 */
-  DSA_FAMILY_KEYS = 5       /* persistent tcgen05/TMEM path for 16 heads per CTA item with the
+  DSA_FAMILY_KEYS = 5,      /* persistent tcgen05/TMEM path for 16 heads per CTA item with the
                                selected keys as the MMA's M dimension (scores and P.V computed
                                transposed); any H % 16 == 0, keys_per_tile 64 */
+  DSA_FAMILY_PAIR_UNION = 6 /* the pair family over blocks of 128 / H queries of one batch row
+                               (H = 16, 32 or 64; SQ a multiple of 128 / H), each block walking
+                               the union of its queries' selected keys with one membership mask
+                               per query; heads_per_cta 128, keys_per_tile 32, split 1 */
 } dsa_family_t;
 
 /* One entry of the shape-keyed launch table (reference: Tuning,
