@@ -23,41 +23,61 @@ namespace {
 
 constexpr int kUnionThreads = 1024;
 constexpr int kKeysPerPass = 4096;
-constexpr int kMaxQpb = 8;  // queries per block (H = 16)
 
-__device__ __forceinline__ uint32_t count_of(const uint32_t* cnt, int key, int q, int qpb) {
-  return (cnt[key * (qpb / 2) + (q >> 1)] >> (16 * (q & 1))) & 0xFFFFu;
-}
+// Counts of one key for QPB queries: QPB / 2 words, 16 bits per query.
+template <int QPB>
+struct KeyCounts {
+  uint32_t w[QPB / 2];
+  __device__ __forceinline__ void load(const uint32_t* cnt, int key) {
+    if constexpr (QPB == 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(cnt + key * 4);
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (QPB == 4) {
+      const uint2 v = *reinterpret_cast<const uint2*>(cnt + key * 2);
+      w[0] = v.x; w[1] = v.y;
+    } else {
+      w[0] = cnt[key];
+    }
+  }
+  __device__ __forceinline__ uint32_t of(int q) const { return (w[q >> 1] >> (16 * (q & 1))) & 0xFFFFu; }
+};
 
-__global__ void __launch_bounds__(kUnionThreads) union_build_kernel(const int32_t* __restrict__ ids, int topk,
-                                                                     int length, int qpb, int32_t* __restrict__ uent,
+template <int QPB>
+__global__ void __launch_bounds__(kUnionThreads, 2) union_build_kernel(const int32_t* __restrict__ ids, int topk,
+                                                                     int length, int32_t* __restrict__ uent,
                                                                      int32_t* __restrict__ ulen, int ucap) {
-  extern __shared__ uint32_t cnt[];  // [kKeysPerPass][qpb / 2]
-  __shared__ int warp_sums[kUnionThreads / 32];
-  __shared__ int base_out;
+  constexpr int kWords = QPB / 2;
+  extern __shared__ __align__(16) uint32_t cnt[];  // [kKeysPerPass][kWords]
+  __shared__ int warp_sums[2][kUnionThreads / 32];  // alternate chunks: two barriers per chunk
   const int blk = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int32_t* bids = ids + (size_t)blk * qpb * topk;  // the block's qpb index rows
+  const int32_t* bids = ids + (size_t)blk * QPB * topk;  // the block's QPB index rows
   int32_t* bent = uent + (size_t)blk * ucap;
-  const int words = kKeysPerPass * (qpb / 2);
-  if (tid == 0) base_out = 0;
+  const int n_ids = QPB * topk;
+  int base_out = 0;  // entries written before this chunk (the same in every thread)
+  int buf = 0;
   for (int k0 = 0; k0 < length; k0 += kKeysPerPass) {
-    for (int i = tid; i < words; i += kUnionThreads) cnt[i] = 0u;
+    for (int i = tid; i < kKeysPerPass * kWords; i += kUnionThreads) cnt[i] = 0u;
     __syncthreads();
-    for (int i = tid; i < qpb * topk; i += kUnionThreads) {
+    const int k1 = min(length, k0 + kKeysPerPass);
+#pragma unroll 4
+    for (int i = tid; i < n_ids; i += kUnionThreads) {
       const int idx = __ldg(bids + i);
-      if (idx >= k0 && idx < length && idx < k0 + kKeysPerPass) {
+      if (idx >= k0 && idx < k1) {
         const int q = i / topk;
-        atomicAdd(&cnt[(idx - k0) * (qpb / 2) + (q >> 1)], 1u << (16 * (q & 1)));
+        atomicAdd(&cnt[(idx - k0) * kWords + (q >> 1)], 1u << (16 * (q & 1)));
       }
     }
     __syncthreads();
     // keys of this pass in ascending order, kUnionThreads at a time
     for (int kb = 0; kb < kKeysPerPass && k0 + kb < length; kb += kUnionThreads) {
       const int key = kb + tid;
+      KeyCounts<QPB> c;
       int m = 0;
       if (k0 + key < length) {
-        for (int q = 0; q < qpb; ++q) m = max(m, (int)count_of(cnt, key, q, qpb));
+        c.load(cnt, key);
+#pragma unroll
+        for (int q = 0; q < QPB; ++q) m = max(m, (int)c.of(q));
       }
       // block-wide exclusive scan of m
       int incl = m;
@@ -66,28 +86,32 @@ __global__ void __launch_bounds__(kUnionThreads) union_build_kernel(const int32_
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
       }
-      if (lane == 31) warp_sums[warp] = incl;
+      // warp_sums[buf] was last read two chunks ago, before the barriers of
+      // the previous chunk that every thread has passed
+      int* ws = warp_sums[buf];
+      if (lane == 31) ws[warp] = incl;
       __syncthreads();
       if (warp == 0) {
-        int s = warp_sums[lane];
+        int s = ws[lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const int v = __shfl_up_sync(0xffffffffu, s, o);
           if (lane >= o) s += v;
         }
-        warp_sums[lane] = s;  // inclusive prefix over warps
+        ws[lane] = s;  // inclusive prefix over warps
       }
       __syncthreads();
-      const int pos = base_out + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - m;
+      const int pos = base_out + (warp > 0 ? ws[warp - 1] : 0) + incl - m;
+      base_out += ws[kUnionThreads / 32 - 1];
+      buf ^= 1;
       for (int e = 0; e < m; ++e) {
         uint32_t bits = 0;
-        for (int q = 0; q < qpb; ++q) bits |= (count_of(cnt, key, q, qpb) > (uint32_t)e ? 1u : 0u) << q;
+#pragma unroll
+        for (int q = 0; q < QPB; ++q) bits |= (c.of(q) > (uint32_t)e ? 1u : 0u) << q;
         if (pos + e < ucap) bent[pos + e] = (int32_t)((uint32_t)(k0 + key) | (bits << 24));
       }
-      __syncthreads();
-      if (tid == 0) base_out += warp_sums[kUnionThreads / 32 - 1];
-      __syncthreads();
     }
+    __syncthreads();  // the next pass clears the counts
   }
   // a block whose queries have no valid index still gets one (fully masked)
   // entry, so that its item has a tile and writes zeros like any other row
@@ -101,18 +125,28 @@ __global__ void __launch_bounds__(kUnionThreads) union_build_kernel(const int32_
   }
 }
 
-}  // namespace
+template <int QPB>
+cudaError_t launch_union_qpb(const int32_t* ids, int topk, int length, int blocks, int32_t* uent, int32_t* ulen,
+                             int ucap, cudaStream_t stream) {
+  const int smem = kKeysPerPass * (QPB / 2) * 4;
+  if (cudaFuncSetAttribute(union_build_kernel<QPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return cudaErrorInvalidConfiguration;
+  union_build_kernel<QPB><<<blocks, kUnionThreads, smem, stream>>>(ids, topk, length, uent, ulen, ucap);
+  return cudaGetLastError();
+}
 
-uint64_t union_smem_bytes(int qpb) { return (uint64_t)kKeysPerPass * (uint64_t)(qpb / 2) * 4u; }
+}  // namespace
 
 cudaError_t launch_union_build(const int32_t* ids, int topk, int length, int qpb, int blocks, int32_t* uent,
                                int32_t* ulen, int ucap, cudaStream_t stream) {
-  if (qpb < 2 || qpb > kMaxQpb || (qpb & 1) || blocks <= 0 || length >= (1 << 24)) return cudaErrorInvalidValue;
-  const int smem = (int)union_smem_bytes(qpb);
-  if (cudaFuncSetAttribute(union_build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return cudaErrorInvalidConfiguration;
-  union_build_kernel<<<blocks, kUnionThreads, smem, stream>>>(ids, topk, length, qpb, uent, ulen, ucap);
-  return cudaGetLastError();
+  if (blocks <= 0 || length >= (1 << 24)) return cudaErrorInvalidValue;
+  switch (qpb) {
+    case 2: return launch_union_qpb<2>(ids, topk, length, blocks, uent, ulen, ucap, stream);
+    case 4: return launch_union_qpb<4>(ids, topk, length, blocks, uent, ulen, ucap, stream);
+    case 8: return launch_union_qpb<8>(ids, topk, length, blocks, uent, ulen, ucap, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace dsa
