@@ -51,10 +51,21 @@ DEFAULT_CONFIG = "prefill_h128"
 # Dominant-kernel DRAM traffic per launch (dram__bytes_read.sum +
 # dram__bytes_write.sum) from the ncu captures summarised under profiles/;
 # None until a capture of that kernel/config exists.
+# Figures are for the uniform index variant and the whole problem on one
+# GPU; a rank of an N-GPU run processes 1/N of the queries.
 TRAFFIC_BYTES = {
-    # profiles/fwd_pair_prefill_h128.md: 356.9 + 59.3 MB (DRAM read + write)
+    # profiles/fwd_pair_prefill_h128.md: 351.3 + 58.0 MB (DRAM read + write)
     # for a 512-query capture of fwd_pair_kernel, scaled to 16384 queries.
-    "prefill_h128": int((356.9e6 + 59.3e6) * 16384 / 512),
+    "prefill_h128": int((351.3e6 + 58.0e6) * 16384 / 512),
+    # profiles/fwd_pair_union_prefill_tp8.md: 32.2 + 0.17 MB for a
+    # 1024-query capture of the union launch's fwd_pair_kernel; the 9.4 MB
+    # L2-resident kv+k_rope is read once whatever the query count, the rest
+    # scales with the queries (x4 for 4096).
+    "prefill_tp8": int((32.2e6 - 9.4e6) * 4096 / 1024 + 9.4e6 + 0.17e6 * 4),
+    # profiles/fwd_stream_prefill_tp8.md: 152.8 + 3.8 MB for a capture of the
+    # stream kernel on 64 queries x 2048 keys at L = 16384, the same gathered
+    # rows per launch as decode_tp8 (only L differs).
+    "decode_tp8": int(152.8e6 + 3.8e6),
     # profiles/fwd_umma_decode_b8.md: 39.07 MB + 0.45 MB, a capture of the
     # full decode_b8 launch of fwd_umma_kernel.
     "decode_b8": int(39.07e6 + 0.45e6),
@@ -515,7 +526,8 @@ def main():
                                 statistics.quantiles(durations, n=10)[-1] if len(durations) > 1 else durations[0]],
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)",
-                     "traffic": TRAFFIC_BYTES.get(args.config)},
+                     "traffic": (TRAFFIC_BYTES[args.config] // world
+                                 if args.config in TRAFFIC_BYTES and args.variant == "uniform" else None)},
         "e2e": {"value": e2e_ms * 1e3, "unit": "us/call", "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": d2h_bytes, "steps": e2e_steps,
                 "mode": "pipelined: inputs in / forward / outputs out on three streams, two buffer sets"},
