@@ -69,6 +69,9 @@ TRAFFIC_BYTES = {
     # profiles/fwd_umma_decode_b8.md: 39.07 MB + 0.45 MB, a capture of the
     # full decode_b8 launch of fwd_umma_kernel.
     "decode_b8": int(39.07e6 + 0.45e6),
+    # profiles/fwd_umma_decode_b1.md: 2,586,368 + 0 bytes, a capture of the
+    # full decode_b1 launch of fwd_umma_kernel.
+    "decode_b1": 2586368,
 }
 
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
