@@ -49,30 +49,47 @@ CONFIGS = {
 DEFAULT_CONFIG = "prefill_h128"
 
 # Dominant-kernel DRAM traffic per launch (dram__bytes_read.sum +
-# dram__bytes_write.sum) from the ncu captures summarised under profiles/;
-# None until a capture of that kernel/config exists.
-# Figures are for the uniform index variant and the whole problem on one
-# GPU; a rank of an N-GPU run processes 1/N of the queries.
-TRAFFIC_BYTES = {
-    # profiles/fwd_pair_prefill_h128.md: 351.3 + 58.0 MB (DRAM read + write)
-    # for a 512-query capture of fwd_pair_kernel, scaled to 16384 queries.
-    "prefill_h128": int((351.3e6 + 58.0e6) * 16384 / 512),
-    # profiles/fwd_pair_union_prefill_tp8.md: 32.2 + 0.17 MB for a
-    # 1024-query capture of the union launch's fwd_pair_kernel; the 9.4 MB
-    # L2-resident kv+k_rope is read once whatever the query count, the rest
-    # scales with the queries (x4 for 4096).
-    "prefill_tp8": int((32.2e6 - 9.4e6) * 4096 / 1024 + 9.4e6 + 0.17e6 * 4),
-    # profiles/fwd_stream_prefill_tp8.md: 152.8 + 3.8 MB for a capture of the
-    # stream kernel on 64 queries x 2048 keys at L = 16384, the same gathered
-    # rows per launch as decode_tp8 (only L differs).
-    "decode_tp8": int(152.8e6 + 3.8e6),
-    # profiles/fwd_umma_decode_b8.md: 39.07 MB + 0.45 MB, a capture of the
-    # full decode_b8 launch of fwd_umma_kernel.
-    "decode_b8": int(39.07e6 + 0.45e6),
-    # profiles/fwd_umma_decode_b1.md: 2,586,368 + 0 bytes, a capture of the
-    # full decode_b1 launch of fwd_umma_kernel.
-    "decode_b1": 2586368,
+# dram__bytes_write.sum) from ncu captures of the default launch on the
+# uniform index variant, as a model of a rank's launch:
+#   traffic = replicated + per_query * (queries of the rank)
+# where `replicated` is what every rank reads whatever its query count (kv
+# rows that stay L2-resident after their first read). The bench reports
+# None for any other variant, shape or launch entry.
+TRAFFIC_MODEL = {
+    # fwd_pair_kernel, 512-query capture of prefill_h128 (one batch row):
+    # 351.3 MB read + 58.0 MB written. kv is re-read from DRAM in proportion
+    # to the queries (75.5 MB of kv per batch row does not stay in the L2
+    # next to the streamed q and outputs), so it all scales per query.
+    "prefill_h128": (0.0, (351.3e6 + 58.0e6) / 512),
+    # union launch's fwd_pair_kernel, 1024-query capture of prefill_tp8:
+    # 32.2 MB read + 0.17 MB written, of which the 9.4 MB kv + k_rope is
+    # read once (it stays L2-resident) and the rest scales with the queries.
+    "prefill_tp8": (9.4e6, (32.2e6 - 9.4e6 + 0.17e6) / 1024),
+    # fwd_stream_kernel, capture of 64 queries x 2048 keys at L = 16384 (the
+    # same gathered rows per launch as decode_tp8; only L differs):
+    # 152.8 MB read + 3.8 MB written.
+    "decode_tp8": (0.0, (152.8e6 + 3.8e6) / 64),
+    # fwd_umma_kernel, capture of the full decode_b8 launch: 39.07 + 0.45 MB.
+    "decode_b8": (0.0, (39.07e6 + 0.45e6) / 16),
+    # fwd_umma_kernel, capture of the full decode_b1 launch: 2,586,368 B read.
+    "decode_b1": (0.0, 2586368.0),
 }
+
+
+def traffic_bytes(config, variant, custom, rank_queries):
+    """Modelled DRAM bytes of one launch of the dominant kernel on a rank
+    (None when no capture covers the workload)."""
+    if custom or variant != "uniform" or config not in TRAFFIC_MODEL:
+        return None
+    replicated, per_query = TRAFFIC_MODEL[config]
+    return int(replicated + per_query * rank_queries)
+
+
+# The CPU oracle (the reference's FP32 math) is timed on the same bounded
+# sample in both arms: the first CPU_SAMPLE_QUERIES flattened queries (all of
+# them when the config has fewer), in chunks of 16 queries for H >= 64 and
+# 128 otherwise, scaled to a full call.
+CPU_SAMPLE_QUERIES = 1024
 
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
@@ -254,24 +271,36 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU reference (oracle) timing
 # ---------------------------------------------------------------------------
-def cpu_reference_rate(data, shape, budget_s, max_rows=None):
-    """Time the oracle on consecutive query rows until ``budget_s`` elapses;
-    returns (seconds per full call, rows timed, threads)."""
-    from oracle import sparse_mla as oracle  # checker/baseline only
+class CpuSample:
+    """The oracle on the bounded CPU sample of a workload (all host threads).
 
-    torch.set_num_threads(os.cpu_count() or 1)
-    b, s, h, _, k = shape
-    total = b * s
-    chunk = max(1, min(total, 16 if h >= 64 else 128))
-    rows_done, elapsed = 0, 0.0
-    while rows_done < total and elapsed < budget_s and (max_rows is None or rows_done < max_rows):
-        rows = list(range(rows_done, min(total, rows_done + chunk)))
-        compact = compact_for_oracle(data, rows)
+    The sample's inputs are copied to the host once (compact per-query
+    copies, identical arithmetic); ``run()`` times one pass of the oracle
+    over the sample and returns the seconds scaled to a full call."""
+
+    def __init__(self, data, shape):
+        from oracle import sparse_mla as oracle  # checker/baseline only
+
+        self.oracle = oracle
+        torch.set_num_threads(os.cpu_count() or 1)
+        b, s, h, _, _ = shape
+        self.total = b * s
+        self.rows = min(self.total, CPU_SAMPLE_QUERIES)
+        chunk = 16 if h >= 64 else 128
+        self.chunks = [compact_for_oracle(data, list(range(r0, min(self.rows, r0 + chunk))))
+                       for r0 in range(0, self.rows, chunk)]
+        self.threads = torch.get_num_threads()
+
+    def run(self):
         t0 = time.perf_counter()
-        oracle.reference_forward(*compact)
-        elapsed += time.perf_counter() - t0
-        rows_done += len(rows)
-    return elapsed / rows_done * total, rows_done, torch.get_num_threads()
+        for compact in self.chunks:
+            self.oracle.reference_forward(*compact)
+        return (time.perf_counter() - t0) * self.total / self.rows
+
+    def describe(self, passes):
+        return (f"first {self.rows} of {self.total} queries ({100.0 * self.rows / self.total:.2f} %) per pass, "
+                f"{passes} timed pass(es) after one untimed pass; FP32 torch oracle of tools/review.py:123-145 "
+                f"(HF32/TF32 off), scaled to a full call")
 
 
 # ---------------------------------------------------------------------------
@@ -299,14 +328,15 @@ def run_reference(args, shape):
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     data = make_device_inputs(shape, SEED, args.variant, dev)
     b, s, h, length, k = shape
-    total = b * s
-    sample_rows = min(total, {16: 512, 32: 256, 64: 128, 128: 64}.get(h, 64))
+    sample = CpuSample(data, shape)
+    data = None
     per_call = []
     for i in range(args.warmup + args.steps):
-        t, rows, threads = cpu_reference_rate(data, shape, budget_s=1e9, max_rows=sample_rows)
+        t = sample.run()
         if i >= args.warmup:
             per_call.append(t)
     us = statistics.mean(per_call) * 1e6
+    threads = sample.threads
     line = {
         "impl": "reference", "metric": METRIC, "value": us, "unit": "us/call", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1e3, "higher_is_better": False,
@@ -314,8 +344,7 @@ def run_reference(args, shape):
         "config": {"workload": args.config, "B": b, "SQ": s, "H": h, "L": length, "TOPK": k,
                    "index_variant": args.variant, "seed": SEED},
         "cpu_baseline": {"value": us, "unit": "us/call", "cores": threads, "kind": "port",
-                         "sample": f"{sample_rows} of {total} queries per step (FP32 torch oracle of "
-                                   f"tools/review.py:123-145, HF32/TF32 off), scaled to a full call"},
+                         "sample": sample.describe(args.steps) + "; one pass per step"},
         "e2e": {"value": us, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -409,11 +438,14 @@ def main():
         clocks.mark(t_host0, time.time())
     durations = [a.elapsed_time(e) for a, e in zip(starts, ends)]  # ms
     total_ms = sum(durations)
+    rank_ms = [total_ms / args.steps]
     if world > 1:
         import torch.distributed as dist
         t = torch.tensor([total_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+        every = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(every, t)
+        rank_ms = [float(x.item()) / args.steps for x in every]
+        total_ms = max(float(x.item()) for x in every)
     ms_per_step = total_ms / args.steps
 
     graph = None  # release the captured graph before the end-to-end part
@@ -529,21 +561,33 @@ def main():
                                 statistics.quantiles(durations, n=10)[-1] if len(durations) > 1 else durations[0]],
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)",
-                     "traffic": (TRAFFIC_BYTES[args.config] // world
-                                 if args.config in TRAFFIC_BYTES and args.variant == "uniform" else None)},
+                     "traffic": traffic_bytes(args.config, args.variant, bool(args.shape or args.tuning), hi - lo),
+                     "traffic_source": "ncu capture of the default launch (uniform indices), modelled per rank"},
         "e2e": {"value": e2e_ms * 1e3, "unit": "us/call", "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": d2h_bytes, "steps": e2e_steps,
                 "mode": "pipelined: inputs in / forward / outputs out on three streams, two buffer sets"},
         "gpu_launches": launches_total,
         "clocks": clocks.summary(),
     }
+    if world > 1:
+        line["ranks"] = {"n": world, "ms_per_step": rank_ms, "min_ms": min(rank_ms), "max_ms": max(rank_ms),
+                         "argmax": max(range(world), key=lambda r: rank_ms[r]),
+                         "queries": [sharded.shard_bounds(b * s, world, r)[1] - sharded.shard_bounds(b * s, world, r)[0]
+                                     for r in range(world)]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dev_data = [t.to(device, non_blocking=True) for t in host_in[0]]  # one GPU: one piece, all queries
         torch.cuda.synchronize()
-        sec, rows, threads = cpu_reference_rate(dev_data, shape, budget_s=args.cpu_budget)
-        line["cpu_baseline"] = {"value": sec * 1e6, "unit": "us/call", "cores": threads, "kind": "port",
-                                "sample": f"first {rows} of {b * s} queries (~{args.cpu_budget:.0f} s), "
-                                          "FP32 torch oracle, scaled to a full call"}
+        sample = CpuSample(dev_data, shape)
+        dev_data = None
+        sample.run()  # untimed pass
+        per_call, spent = [], 0.0
+        while spent < args.cpu_budget or not per_call:
+            t0 = time.perf_counter()
+            per_call.append(sample.run())
+            spent += time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": statistics.mean(per_call) * 1e6, "unit": "us/call",
+                                "cores": sample.threads, "kind": "port",
+                                "sample": sample.describe(len(per_call)) + f" (~{args.cpu_budget:.0f} s)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -3,9 +3,10 @@
 Drop-in for ``dsa.forward`` (dsa/__init__.py:2-5 of the reference):
 ``import dsa_b200 as dsa; dsa.forward(q, kv, q_rope, k_rope, indices)``.
 """
-from .api import ForwardPlan, device_status, forward
+from .api import ForwardPlan, check_device_status, clear_device_status, device_status, forward
 from .config import CASE_SHAPES, SELECTED, Tuning
 from .sparse_flash_attention import npu_sparse_flash_attention, sparse_flash_attention
 
 __all__ = ["forward", "ForwardPlan", "Tuning", "CASE_SHAPES", "SELECTED", "device_status",
-           "sparse_flash_attention", "npu_sparse_flash_attention"]
+           "check_device_status", "clear_device_status", "sparse_flash_attention",
+           "npu_sparse_flash_attention"]

@@ -40,6 +40,7 @@ EXPORTS = (
     "dsa_merge_partials",
     "dsa_last_launch_count",
     "dsa_sparse_mla_fwd_noalloc",
+    "dsa_set_wait_test",
 )
 
 # Byte size of the built-in scratch array of dsa_sparse_mla_fwd_noalloc
@@ -99,6 +100,8 @@ def load():
         lib.dsa_last_launch_count.restype = ctypes.c_int
         lib.dsa_sparse_mla_fwd_noalloc.restype = ctypes.c_int
         lib.dsa_sparse_mla_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+        lib.dsa_set_wait_test.restype = ctypes.c_int
+        lib.dsa_set_wait_test.argtypes = [ctypes.c_uint64, ctypes.c_int]
         version = lib.dsa_abi_version()
         if version != ABI_VERSION:
             raise RuntimeError(f"libdsa_b200.so ABI {version} != expected {ABI_VERSION}; rebuild it")
@@ -112,7 +115,7 @@ def status_string(code: int) -> str:
 
 def raise_for_status(code: int, what: str) -> None:
     """Map a dsa_status_t to the reference's exception types (ValueError for
-    argument/config problems, dsa/api.py:27-42; RuntimeError otherwise)."""
+    argument/config problems, dsa/api.py:22-37; RuntimeError otherwise)."""
     if code == STATUS_OK:
         return
     msg = f"{what}: {status_string(code)} (status {code})"

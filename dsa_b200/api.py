@@ -1,7 +1,7 @@
 """Public entry point: check inputs, pick the launch entry, allocate, launch.
 
-Mirrors ``forward`` of CHNJZ/dsa (dsa/api.py:81-137) on CUDA tensors:
-same signature, same input contract (dsa/api.py:23-43), same outputs and the
+Mirrors ``forward`` of CHNJZ/dsa (dsa/api.py:76-132) on CUDA tensors:
+same signature, same input contract (dsa/api.py:18-38), same outputs and the
 same exception types. The device work is the sm_100a library
 (libdsa_b200.so, include/dsa_b200.h) reached through ctypes; there is no
 Python, Triton or CPU fallback.
@@ -29,7 +29,7 @@ _FAMILY_NAMES = {_native.FAMILY_WARP_MMA: "warp_mma", _native.FAMILY_UMMA: "umma
 
 
 def _check_inputs(q, kv, q_rope, k_rope, indices):
-    """Shape/device/contiguity/dtype contract of dsa/api.py:23-43."""
+    """Shape/device/contiguity/dtype contract of dsa/api.py:18-38."""
     q_shape, kv_shape, ids_shape = q.shape, kv.shape, indices.shape
     if len(q_shape) != 4 or len(kv_shape) != 4 or len(ids_shape) != 4:
         raise ValueError("q, kv and indices must be 4-D tensors")
@@ -53,7 +53,7 @@ def _check_inputs(q, kv, q_rope, k_rope, indices):
 
 
 def _check_cores(cores):
-    # Accepted for source compatibility (dsa/api.py:81, :99-100); the grid is
+    # Accepted for source compatibility (dsa/api.py:76, :94-95); the grid is
     # sized from the device's SM count, so the value is only validated.
     if type(cores) is not int or cores <= 0:
         raise ValueError("cores must be a positive int")
@@ -77,7 +77,7 @@ def _check_scale(scale):
 
 
 def _check_tuning(config, shape, cores):
-    """Launch-entry checks: the reference's field rules (dsa/api.py:46-65)
+    """Launch-entry checks: the reference's field rules (dsa/api.py:41-60)
     plus what the sm_100a kernels support (dsa_check_launch)."""
     if not isinstance(config, Tuning):
         raise TypeError("config must be a dsa_b200.Tuning")
@@ -139,13 +139,33 @@ def _status_word(device):
     return word
 
 
+def _device_arg(device):
+    return torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+
+
 def device_status(device=None) -> int:
     """Synchronise and return the OR of device error bits reported so far
     (1 = a bounded device-side wait timed out)."""
-    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    device = _device_arg(device)
     word = _status_word(device)
     torch.cuda.synchronize(device)
     return int(word.item())
+
+
+def check_device_status(device=None) -> None:
+    """Synchronise and raise ``RuntimeError`` (the C ABI's
+    DSA_STATUS_DEVICE_TIMEOUT) if a kernel reported an error bit."""
+    bits = device_status(device)
+    if bits:
+        raise RuntimeError(f"sparse-MLA kernel: {_native.status_string(_native.STATUS_DEVICE_TIMEOUT)} "
+                           f"(device error bits {bits:#x})")
+
+
+def clear_device_status(device=None) -> None:
+    """Reset the device error word (kernels only ever set bits in it)."""
+    device = _device_arg(device)
+    _status_word(device).zero_()
+    torch.cuda.synchronize(device)
 
 
 def _launch_native(args, stream_handle):
@@ -171,7 +191,7 @@ def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_ker
     fixes 1/24 and notes that a model keeps its own scale, README.md:81-84).
     Duplicate indices keep their repeated weight; indices outside [0, L) are
     masked. The reference requires at least one valid index per query
-    (dsa/api.py:82-91); here a (query, head) row without one gets output 0,
+    (dsa/api.py:77-86); here a (query, head) row without one gets output 0,
     softmax_max -inf and softmax_sum 0.
 
     ``config`` overrides the shape-keyed launch entry; ``cores`` is validated
@@ -210,13 +230,23 @@ def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_ker
     count = _launch_native(args, stream)
     result = (output, maximum, denominator)
     if return_kernels:
-        name = "dsa_fwd_" + _FAMILY_NAMES.get(launch.family, str(launch.family))
-        records = [LaunchRecord(name, launch.family, launch.heads_per_cta, launch.keys_per_tile, launch.split)]
-        if count > 1:
-            records.append(LaunchRecord("dsa_merge", launch.family, launch.heads_per_cta,
-                                        launch.keys_per_tile, launch.split))
-        return result, tuple(records)
+        return result, _launch_records(launch, count)
     return result
+
+
+def _launch_records(launch, count):
+    """Descriptors of the kernels one call enqueued, in launch order: the
+    union build before the union launch's pair kernel; the split merge after
+    a main kernel with split > 1."""
+    name = "dsa_fwd_" + _FAMILY_NAMES.get(launch.family, str(launch.family))
+    fields = (launch.family, launch.heads_per_cta, launch.keys_per_tile, launch.split)
+    if launch.family == _native.FAMILY_PAIR_UNION:
+        names = ["dsa_union_build", name]
+    else:
+        names = [name] + (["dsa_merge"] if launch.split > 1 else [])
+    if len(names) != count:
+        raise RuntimeError(f"library enqueued {count} kernels, expected {names}")
+    return tuple(LaunchRecord(n, *fields) for n in names)
 
 
 class ForwardPlan:

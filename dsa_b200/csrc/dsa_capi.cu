@@ -1,13 +1,14 @@
 // extern "C" boundary of libdsa_b200.so (declared in include/dsa_b200.h).
 //
 // Host-side orchestration of one forward call, the C++ counterpart of the
-// reference's forward (dsa/api.py:81-137): pick or check the launch entry,
+// reference's forward (dsa/api.py:76-132): pick or check the launch entry,
 // carve the split partials out of the caller's workspace, launch the main
 // kernel and, for split > 1, the FP32 merge. Input validation of shapes and
 // dtypes happens in the Python mirror (dsa_b200/api.py); here only what the
 // C ABI can see is checked (null pointers, sizes, alignment, launch entry).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 
@@ -17,6 +18,10 @@
 namespace {
 
 thread_local int g_last_launch_count = 0;
+
+// Failure-path test settings of dsa_set_wait_test (process-wide).
+std::atomic<unsigned long long> g_wait_limit_ns{0};
+std::atomic<int> g_wait_test{0};
 
 constexpr uint64_t kAlign = 256;
 inline uint64_t align_up(uint64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
@@ -69,6 +74,11 @@ UnionLayout union_layout(int64_t tokens, int64_t heads, int64_t topk) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Largest TOPK of the union launch: union_build_kernel keeps each query's
+// count of a key in a 16-bit half-word, and (128 / H) * TOPK entries per
+// block must fit an int.
+constexpr int64_t kUnionMaxTopk = 65535;
+
 }  // namespace
 
 extern "C" {
@@ -112,6 +122,8 @@ int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t leng
       if (launch->heads_per_cta != 128 || bn != 32 || launch->split != 1) return DSA_STATUS_UNSUPPORTED;
       if (heads != 16 && heads != 32 && heads != 64) return DSA_STATUS_UNSUPPORTED;
       if (queries % (128 / heads) != 0 || length >= (1 << 24)) return DSA_STATUS_UNSUPPORTED;
+      // the union build counts a key's repeats per query in 16 bits
+      if (topk > kUnionMaxTopk) return DSA_STATUS_UNSUPPORTED;
       break;
     }
     case DSA_FAMILY_UMMA:
@@ -167,7 +179,7 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
   // clusters and the keys are dense enough (L <= 4 TOPK: the union of 8
   // queries' keys is then at most ~3.6 TOPK, against 8 TOPK key-rows for the
   // per-query form)
-  if (heads == 16 && queries % 8 == 0 && length <= 4 * topk && length < (1 << 24)) {
+  if (heads == 16 && queries % 8 == 0 && length <= 4 * topk && length < (1 << 24) && topk <= kUnionMaxTopk) {
     const int pair_ctas = dsa::pair_max_ctas();
     if (pair_ctas > 0 && batch * queries / 8 >= pair_ctas / 2) {
       e.family = DSA_FAMILY_PAIR_UNION;
@@ -265,6 +277,8 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
   p.keys_per_tile = e.keys_per_tile;
   p.heads_per_cta = e.heads_per_cta;
   if (!dsa::fill_scale(a->scale, p)) return DSA_STATUS_BAD_ARGUMENT;
+  p.wait_limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  p.wait_test = g_wait_test.load(std::memory_order_relaxed);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err = cudaSuccess;
@@ -325,5 +339,11 @@ int dsa_merge_partials(const float* numerator, const float* partial_max, const f
 }
 
 int dsa_last_launch_count(void) { return g_last_launch_count; }
+
+int dsa_set_wait_test(uint64_t limit_ns, int stall) {
+  g_wait_limit_ns.store((unsigned long long)limit_ns, std::memory_order_relaxed);
+  g_wait_test.store(stall != 0 ? 1 : 0, std::memory_order_relaxed);
+  return DSA_STATUS_OK;
+}
 
 }  // extern "C"

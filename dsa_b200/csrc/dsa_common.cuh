@@ -1,13 +1,13 @@
 // Shared definitions for the sm_100a sparse-MLA forward kernels.
 //
-// Layout facts used everywhere (reference contract, dsa/api.py:23-43):
+// Layout facts used everywhere (reference contract, dsa/api.py:18-38):
 //   q      [T, H, 512]  bf16, T = B*SQ flattened tokens (batch-major)
 //   q_rope [T, H, 64]   bf16
 //   kv     [B, L, 512]  bf16 (the size-1 head axis is dropped)
 //   k_rope [B, L, 64]   bf16
 //   ids    [T, TOPK]    int32
 //   out    [T, H, 512]  bf16; max/sum [T, H] fp32 (== [B,1,SQ,H] contiguous)
-//   split-KV partials (dsa/api.py:116-118): numerator [T, S, H, 512] fp32,
+//   split-KV partials (dsa/api.py:111-113): numerator [T, S, H, 512] fp32,
 //   partial max/sum [T, S, H] fp32.
 #pragma once
 
@@ -56,6 +56,11 @@ struct FwdParams {
   // scale_log2 = log2(e) / scale_div.
   float scale_div;
   float scale_log2;
+  // Bound of each device-side wait of the split-V family in ns (0: the
+  // built-in 2 s); wait_test != 0 makes that family's first CTA wait on a
+  // barrier nothing arrives at, so the bound runs out (failure-path test).
+  unsigned long long wait_limit_ns;
+  int wait_test;
 };
 
 // Host: fill scale_div / scale_log2 from the ABI's scale (0 = the

@@ -85,7 +85,9 @@ enum Bar {
   kPvDone0 = kPFull0 + 2,          // PV of tiles g with g % 2 == b done (P buffer b free)
   kEpiGo = kPvDone0 + 2,           // the item's last PV is done and (l, f) are posted (softmax warps)
   kOFree,                          // the QK issuers have read their part of O (next item's PV may start)
-  kBarCount
+  kStall,                          // failure-path test: nothing ever arrives here
+  kDrain0,                         // abort path: MMA issuer k's issued MMAs have completed
+  kBarCount = kDrain0 + kQkIssuers + 1
 };
 constexpr uint32_t kOffTmemSlot = kOffBar + kBarCount * 8u;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 8u;
@@ -163,9 +165,10 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Bounded wait whose result is the same in every lane of the warp.
-__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, volatile int* abort) {
-  const bool ok = mbar_wait(bar, parity, abort);
+// Bounded wait (limit_ns) whose result is the same in every lane of the warp.
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          unsigned long long limit_ns) {
+  const bool ok = mbar_wait(bar, parity, abort, false, limit_ns);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
@@ -221,6 +224,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
   const int lane = threadIdx.x & 31;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sbase + kOffAbort);
   auto bar = [&](int i) -> uint32_t { return base + kOffBar + 8u * (uint32_t)i; };
+  const unsigned long long lim = p.wait_limit_ns != 0 ? p.wait_limit_ns : kWaitLimitNs;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUmStages; ++s) {
@@ -240,6 +244,8 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     }
     mbar_init(bar(kEpiGo), kSoftWarps);
     mbar_init(bar(kOFree), kQkIssuers);
+    mbar_init(bar(kStall), 1);
+    for (int k = 0; k <= kQkIssuers; ++k) mbar_init(bar(kDrain0 + k), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -258,7 +264,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
   // Columns 128..255 of O for the item's head rows in TMEM lane quadrant
   // warp % 4, by an issuer warp once the softmax warps post the item's (l, f).
   auto epilogue_upper_half = [&](const Item& w, uint32_t it) -> bool {
-    if (!wait_warp(bar(kEpiGo), it & 1u, abort_flag)) return false;
+    if (!wait_warp(bar(kEpiGo), it & 1u, abort_flag, lim)) return false;
     tc_fence_after();
     const int row = (warp & 3) * 32 + lane;
     const float2 lf = epi[row];
@@ -289,7 +295,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     bool ok = true;
     while (cur.item < n_items) {
       if (n > 0) {  // the stage's previous tile has been consumed by its PV
-        if (lane == 0) ok = mbar_wait(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag);
+        if (lane == 0) ok = mbar_wait(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag, false, lim);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
       }
@@ -339,7 +345,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       const Item w = make_item(p, item);
       // Every issuer observes every item's Q (even without a tile in it) and
       // acknowledges, so no issuer can fall a barrier phase behind.
-      ok = wait_warp(bar(kQFull), it & 1u, abort_flag);
+      ok = wait_warp(bar(kQFull), it & 1u, abort_flag, lim);
       if (!ok) break;
       if (elect_one()) mbar_arrive(bar(kQSeen));
       __syncwarp();
@@ -350,9 +356,9 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         // tile (g - 4, another issuer's). Once the gather of tile g has
         // started, that phase has completed and the parity wait refers to
         // tile g's phase exactly.
-        ok = wait_word_warp(reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile) + s, g, abort_flag);
-        if (ok) ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
-        if (ok && n > 0) ok = wait_warp(bar(kSFree0 + i), (n - 1) & 1u, abort_flag);
+        ok = wait_word_warp(reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile) + s, g, abort_flag, lim);
+        if (ok) ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag, lim);
+        if (ok && n > 0) ok = wait_warp(bar(kSFree0 + i), (n - 1) & 1u, abort_flag, lim);
         if (!ok) break;
         tc_fence_after();
         const uint32_t stage = base + kOffK + s * kKStage;
@@ -390,10 +396,10 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       const Item w = make_item(p, item);
       const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
       for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
-        ok = wait_warp(bar(kPFull0 + (g & 1u)), (g >> 1) & 1u, abort_flag);
+        ok = wait_warp(bar(kPFull0 + (g & 1u)), (g >> 1) & 1u, abort_flag, lim);
         // the first PV of an item overwrites O: the previous item's epilogue
         // (the QK issuers' part) must have read it
-        if (ok && t == 0 && it > 0) ok = wait_warp(bar(kOFree), (it - 1) & 1u, abort_flag);
+        if (ok && t == 0 && it > 0) ok = wait_warp(bar(kOFree), (it - 1) & 1u, abort_flag, lim);
         if (!ok) break;
         tc_fence_after();
         const uint32_t stage = base + kOffK + (g % kUmStages) * kKStage;
@@ -424,11 +430,17 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
+      if (it == 0 && p.wait_test != 0 && blockIdx.x == 0) {
+        // failure-path test: wait on a barrier that nothing arrives at, so the
+        // bounded wait runs out and the whole CTA takes its abort path
+        ok = wait_warp(bar(kStall), 0u, abort_flag, lim);
+        if (!ok) break;
+      }
       // Q of this head row: dims 0..319 -> TMEM, dims 320..511 and the rope
       // dims -> shared memory (128-byte swizzle). The previous item's MMAs
       // are complete (its epilogue waited for its last PV), and every QK
       // issuer has seen the previous item's Q.
-      if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag))) break;
+      if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag, lim))) break;
       {
         const size_t qrow = (size_t)w.token * kUmHeads + row;
         const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
@@ -475,7 +487,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         const uint32_t s = g % kUmStages;
         const uint32_t i = g % kQkIssuers;
         const uint32_t n = g / kQkIssuers;  // uses of S buffer i so far
-        ok = wait_warp(bar(kSFull0 + i), n & 1u, abort_flag);
+        ok = wait_warp(bar(kSFull0 + i), n & 1u, abort_flag, lim);
         if (!ok) break;
         tc_fence_after();
         float x[32];
@@ -490,7 +502,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kSFree0 + i));
         // validity bits of the tile's keys (written by the gather warp)
-        ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag);
+        ok = wait_warp(bar(kFull0 + s), (g / kUmStages) & 1u, abort_flag, lim);
         if (!ok) break;
         const uint32_t mbits = mask_all[s];
         float mx = -INFINITY;
@@ -520,7 +532,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         l = l * alpha + sum;
         // P buffer g % 2 is free once PV(g - 2) finished reading it
         const uint32_t pb = g & 1u;
-        if (g >= 2) ok = wait_warp(bar(kPvDone0 + pb), ((g >> 1) - 1) & 1u, abort_flag);
+        if (g >= 2) ok = wait_warp(bar(kPvDone0 + pb), ((g >> 1) - 1) & 1u, abort_flag, lim);
         if (!ok) break;
         uint8_t* const prow = prow0 + pb * kPBytes;
 #pragma unroll
@@ -530,7 +542,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         fence_proxy_async_smem();
         if (__any_sync(0xffffffffu, resc) && t > 0) {
           // O is read and rescaled: PV(g - 1) must have finished writing it
-          ok = wait_warp(bar(kPvDone0 + (pb ^ 1u)), ((g - 1) >> 1) & 1u, abort_flag);
+          ok = wait_warp(bar(kPvDone0 + (pb ^ 1u)), ((g - 1) >> 1) & 1u, abort_flag, lim);
           if (!ok) break;
           tc_fence_after();
           uint32_t o[32];
@@ -552,7 +564,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       if (!ok) break;
       // ---- epilogue: columns 0..127 of this CTA's 256 dims of the head row
       // (the issuer warp of this lane quadrant writes 128..255) ----
-      ok = wait_warp(bar(kPvDone0 + ((g - 1) & 1u)), ((g - 1) >> 1) & 1u, abort_flag);
+      ok = wait_warp(bar(kPvDone0 + ((g - 1) & 1u)), ((g - 1) >> 1) & 1u, abort_flag, lim);
       if (!ok) break;
       const float f = (m_true == kNegFltMax) ? 1.f : ex2((m_used - m_true) * c);
       epi[row] = make_float2(l, f);
@@ -580,6 +592,23 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  if (*abort_flag) {
+    // Abort path: a role gave up, so MMAs an issuer warp enqueued may still be
+    // running (on the normal path the softmax and epilogue waits have seen
+    // every one complete). Each issuer commits once more and waits, bounded,
+    // until its MMAs have completed before the TMEM they write is released.
+    // elect.sync elects the same lane of a converged warp as at issue time.
+    if (warp >= kQkWarp0 && warp <= kPvWarp) {
+      const uint32_t k = (uint32_t)(warp - kQkWarp0);
+      tc_fence_after();
+      if (elect_one()) mma_commit(bar(kDrain0 + k));
+      __syncwarp();
+      const bool drained = mbar_wait_drain(bar(kDrain0 + k), 0u);
+      if (!drained && lane == 0) report_error(p.status, kErrTimeout);
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

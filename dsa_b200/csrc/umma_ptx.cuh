@@ -1,8 +1,9 @@
 // Inline-PTX wrappers for the sm_100a tcgen05 / bulk-copy / cluster path.
 //
 // Every spin on an mbarrier is bounded (kWaitLimitNs of wall time read from
-// %globaltimer); a wait that gives up returns false and the caller reports
-// kErrTimeout through the status word instead of trapping.
+// %globaltimer unless the launch gives another limit); a wait that gives up
+// returns false and the caller reports kErrTimeout through the status word
+// instead of trapping.
 #pragma once
 
 #include <cuda.h>
@@ -78,8 +79,10 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait; `abort` is a shared flag other roles set after a timeout.
+// The wait gives up `limit_ns` after its 16th unsuccessful try.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          bool cluster_scope = false) {
+                                          bool cluster_scope = false,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   unsigned long long start = 0;
   for (uint32_t it = 0;; ++it) {
     if (cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
@@ -87,7 +90,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       if (*abort) return false;
       const unsigned long long now = global_ns();
       if (start == 0) start = now;
-      else if (now - start > kWaitLimitNs) {
+      else if (now - start > limit_ns) {
         *abort = 1;
         return false;
       }
@@ -95,9 +98,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Bounded wait (kWaitLimitNs) that ignores the abort flag: used on the abort
+// path itself, for completions that always arrive (a tcgen05.commit of
+// tensor-core work already issued).
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  unsigned long long start = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 15u) {
+      const unsigned long long now = global_ns();
+      if (start == 0) start = now;
+      else if (now - start > kWaitLimitNs) return false;
+    }
+  }
+}
+
 // Bounded wait (lane 0 polls) until a shared word equals `value`; the same
 // result in every lane of the warp.
-__device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t value, volatile int* abort) {
+__device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t value, volatile int* abort,
+                                               unsigned long long limit_ns = kWaitLimitNs) {
   bool ok = true;
   if ((threadIdx.x & 31) == 0 && *word != value) {
     const unsigned long long start = global_ns();
@@ -107,7 +126,7 @@ __device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t
           ok = false;
           break;
         }
-        if (global_ns() - start > kWaitLimitNs) {
+        if (global_ns() - start > limit_ns) {
           *abort = 1;
           ok = false;
           break;

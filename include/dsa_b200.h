@@ -6,8 +6,8 @@
  *
  *     forward(q, kv, q_rope, k_rope, indices) -> (output, softmax_max, softmax_sum)
  *
- * (reference: dsa/api.py:81-137). Shapes, dtypes and semantics are the
- * reference's (dsa/api.py:23-43, dsa/api.py:82-91):
+ * (reference: dsa/api.py:76-132). Shapes, dtypes and semantics are the
+ * reference's (dsa/api.py:18-38, dsa/api.py:77-86):
  *
  *   q        BF16  [B, SQ, H, 512]   contiguous
  *   kv       BF16  [B, L, 1, 512]    contiguous (shared key and value)
@@ -23,7 +23,7 @@
  *
  * A (token, head) row whose indices are all outside [0, L) gets output 0,
  * softmax_max -inf and softmax_sum 0 (the reference requires at least one
- * valid index per query and leaves this case undefined, dsa/api.py:82-91).
+ * valid index per query and leaves this case undefined, dsa/api.py:77-86).
  *
  * Every pointer is a device pointer on the current device. No function
  * allocates device memory: temporaries (split-KV partials) live in a
@@ -54,7 +54,7 @@ extern "C" {
 
 /* Status codes. The Python wrapper maps BAD_ARGUMENT/UNSUPPORTED to
  * ValueError and the rest to RuntimeError, as the reference raises
- * ValueError for shape/config problems (dsa/api.py:27-42, 97). */
+ * ValueError for shape/config problems (dsa/api.py:22-37, 92). */
 typedef enum dsa_status {
   DSA_STATUS_OK = 0,
   DSA_STATUS_BAD_ARGUMENT = 1,      /* null pointer, non-positive size, misaligned buffer */
@@ -66,7 +66,7 @@ typedef enum dsa_status {
 } dsa_status_t;
 
 /* Kernel families of the sm_100a launch table (replaces the reference's
- * workspace/ragged kernel choice, dsa/api.py:120-128). */
+ * workspace/ragged kernel choice, dsa/api.py:115-123). */
 typedef enum dsa_family {
   DSA_FAMILY_AUTO = 0,      /* pick by shape (dsa_default_launch) */
   DSA_FAMILY_WARP_MMA = 1,  /* generic: 16 heads per CTA, warp-level MMA, any H % 16 == 0 */
@@ -86,7 +86,7 @@ typedef enum dsa_family {
 } dsa_family_t;
 
 /* One entry of the shape-keyed launch table (reference: Tuning,
- * dsa/config.py:10-19, and its constraints dsa/api.py:46-65). */
+ * dsa/config.py:10-19, and its constraints dsa/api.py:41-60). */
 typedef struct dsa_launch {
   int32_t family;          /* dsa_family_t */
   int32_t heads_per_cta;   /* BM: heads sharing one gathered tile in one CTA */
@@ -96,7 +96,7 @@ typedef struct dsa_launch {
 } dsa_launch_t;
 
 /* Arguments of one forward call (reference: forward's tensors and the
- * kernel arguments of dsa/api.py:120-133). */
+ * kernel arguments of dsa/api.py:115-128). */
 typedef struct dsa_fwd_args {
   const void* q;            /* BF16 [B,SQ,H,512] */
   const void* kv;           /* BF16 [B,L,1,512] */
@@ -125,24 +125,24 @@ DSA_B200_API int dsa_abi_version(void);
 DSA_B200_API const char* dsa_status_string(int status);
 
 /* Shape-keyed default launch entry (replaces the import-time validated
- * table _DEFAULT_CONFIGS, dsa/api.py:68-78, and config.select,
+ * table _DEFAULT_CONFIGS, dsa/api.py:63-73, and config.select,
  * dsa/config.py:64-69). Depends only on the shape and the SM count of the
  * current device, never on input values. Returns DSA_STATUS_OK. */
 DSA_B200_API int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t length,
                        int64_t topk, dsa_launch_t* out);
 
 /* Check a launch entry against a shape (replaces _check_tuning,
- * dsa/api.py:46-65). Returns OK or UNSUPPORTED. */
+ * dsa/api.py:41-60). Returns OK or UNSUPPORTED. */
 DSA_B200_API int dsa_check_launch(int64_t batch, int64_t queries, int64_t heads, int64_t length,
                      int64_t topk, const dsa_launch_t* launch);
 
 /* Workspace bytes the call needs (replaces the per-call torch.empty of the
- * GM workspace and the split partials, dsa/api.py:107-118). Returns 0 for
+ * GM workspace and the split partials, dsa/api.py:102-113). Returns 0 for
  * split == 1 and for an invalid entry. */
 DSA_B200_API uint64_t dsa_fwd_workspace_bytes(const dsa_fwd_args_t* args);
 
 /* The forward: main kernel and, when split > 1, the FP32 merge, both
- * enqueued on `stream` (reference: forward, dsa/api.py:81-137).
+ * enqueued on `stream` (reference: forward, dsa/api.py:76-132).
  * Returns a dsa_status_t. */
 DSA_B200_API int dsa_sparse_mla_fwd(const dsa_fwd_args_t* args, void* stream);
 
@@ -156,8 +156,21 @@ DSA_B200_API int dsa_merge_partials(const float* numerator, const float* partial
                        void* stream);
 
 /* Number of kernels the last successful dsa_sparse_mla_fwd on this host
- * thread enqueued (1 or 2), for launch accounting. */
+ * thread enqueued (1 or 2), for launch accounting. Calls of
+ * dsa_sparse_mla_fwd_noalloc do not update it. */
 DSA_B200_API int dsa_last_launch_count(void);
+
+/* Test hook of the device-side failure path (no counterpart in the
+ * reference, which bounds a hung run with a host-side watchdog,
+ * tools/review.py:298-299). Applies to later launches of the split-V family
+ * (DSA_FAMILY_UMMA) from this process; every other family keeps its fixed
+ * 2 s bound. limit_ns bounds each device-side wait (0 restores the built-in
+ * 2 s). stall != 0 makes the first CTA of each launch wait on a barrier that
+ * nothing arrives at: that wait runs out, the CTA ORs the timeout bit (1)
+ * into the status word, waits for the tensor-core work it already issued,
+ * releases its tensor memory and leaves, and the launch completes (the
+ * outputs of that CTA's items are then undefined). Returns DSA_STATUS_OK. */
+DSA_B200_API int dsa_set_wait_test(uint64_t limit_ns, int stall);
 
 /* Size of the library's built-in scratch array used by
  * dsa_sparse_mla_fwd_noalloc (32 MiB, held on every GPU that loads the

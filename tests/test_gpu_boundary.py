@@ -23,20 +23,22 @@ def _gpu(data):
     return [t.cuda() for t in data]
 
 
-def _check(got, ref, gates=oracle.GATES):
+def _check(got, ref, gates=(oracle.GATES, oracle.ELEMENT_GATES)):
     metrics = oracle.accuracy([t.float().cpu() for t in got], ref)
-    assert oracle.passes(metrics, gates), metrics
+    assert oracle.passes(metrics, *gates), metrics
 
 
 def _scaled_gates(scale):
-    """The statistics gate (1e-5) is stated at the reference's scale 1/24. A
+    """The statistics gates (1e-5, max-normalised and element-wise) are
+    stated at the reference's scale 1/24. A
     raw score differs from the oracle's by its FP32 accumulation order
     (~1e-5 absolute for 576-term dot products of N(0,1) values), and the
     scale multiplies that difference into every exponent, so the gate on max
     and sum grows with 24 * scale; the output gate is unchanged."""
     k = max(1.0, 24.0 * scale)
-    return {"output": oracle.GATES["output"], "maximum": oracle.GATES["maximum"] * k,
-            "denominator": oracle.GATES["denominator"] * k}
+    gates = {"output": oracle.GATES["output"], "maximum": oracle.GATES["maximum"] * k,
+             "denominator": oracle.GATES["denominator"] * k}
+    return gates, {name: g * k for name, g in oracle.ELEMENT_GATES.items()}
 
 
 @pytest.mark.parametrize("split", [1, 3])

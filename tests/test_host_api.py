@@ -13,7 +13,11 @@ import pytest
 import torch
 
 import dsa_b200
-from dsa_b200 import api, config
+from dsa_b200 import _native, api, config
+
+
+def _native_family_union():
+    return _native.FAMILY_PAIR_UNION
 
 
 @pytest.fixture()
@@ -26,7 +30,7 @@ def meta_api(monkeypatch):
         events.append(("launch", args.batch, args.queries, args.heads, args.length, args.topk,
                        args.launch.family, args.launch.keys_per_tile, args.launch.split,
                        args.workspace_bytes))
-        return 2 if args.launch.split > 1 else 1
+        return 2 if args.launch.split > 1 or args.launch.family == _native_family_union() else 1
 
     monkeypatch.setattr(api, "_launch_native", launch)
     return events
@@ -111,7 +115,7 @@ def test_explicit_tuning_accepted(meta_api):
 
 
 def test_unknown_shape_uses_heuristic(meta_api):
-    """Deliberate difference from the reference (dsa/api.py:93-97 raises for a
+    """Deliberate difference from the reference (dsa/api.py:88-92 raises for a
     shape outside its 16-entry table): any shape meeting the input contract
     gets a shape-only launch entry."""
     dsa_b200.forward(*data_for((4, 2, 32, 8192, 2048)))
@@ -128,3 +132,16 @@ def test_ragged_topk_accepted(meta_api):
 def test_head_count_must_be_multiple_of_16(meta_api):
     with pytest.raises(ValueError):
         dsa_b200.forward(*data_for((1, 1, 24, 1024, 64)))
+
+
+def test_dsa_package_shim(meta_api):
+    """``import dsa; dsa.forward(...)`` works literally, as for the reference
+    package (dsa/__init__.py:2-5), and runs this library's forward."""
+    import dsa
+
+    assert dsa.forward is dsa_b200.forward
+    assert dsa.Tuning is dsa_b200.Tuning
+    assert dsa.CASE_SHAPES is dsa_b200.CASE_SHAPES and dsa.SELECTED is dsa_b200.SELECTED
+    assert set(dsa.__all__) == {"forward", "Tuning", "CASE_SHAPES", "SELECTED"}
+    out, mx, sm = dsa.forward(*data_for((1, 2, 32, 1024, 256)))
+    assert out.shape == (1, 2, 32, 512) and mx.shape == (1, 1, 2, 32) and len(meta_api) == 1

@@ -82,3 +82,22 @@ def test_forward_fails_loudly_without_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "missing.so"))
     with pytest.raises(RuntimeError, match="no fallback"):
         _native.load()
+
+
+def test_union_launch_topk_bound():
+    """The union launch counts a key's repeats per query in 16 bits: TOPK
+    above 65535 is refused for it (and the default never picks it then)."""
+    lib = _native.load()
+    union = _native.Launch(_native.FAMILY_PAIR_UNION, 128, 32, 1)
+    assert lib.dsa_check_launch(1, 8, 16, 1 << 20, 65535, ctypes.byref(union)) == 0
+    assert lib.dsa_check_launch(1, 8, 16, 1 << 20, 65536, ctypes.byref(union)) == _native.STATUS_UNSUPPORTED
+    e = _native.Launch()
+    assert lib.dsa_default_launch(1, 8192, 16, 200000, 65536, ctypes.byref(e)) == 0
+    assert e.family != _native.FAMILY_PAIR_UNION
+
+
+def test_wait_test_hook_is_host_only():
+    """The failure-path test hook only sets host-side values for later launches."""
+    lib = _native.load()
+    assert lib.dsa_set_wait_test(1000, 1) == 0
+    assert lib.dsa_set_wait_test(0, 0) == 0

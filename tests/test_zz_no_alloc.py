@@ -6,9 +6,9 @@ not pay cudaFree's device-wide synchronisation, or an FFI host that only owns
 the input and output buffers. For them the library keeps the split-KV
 partials in its own fixed-size device array instead of a caller workspace.
 
-This test calls the variant through the C ABI twice in a row, with different
-shapes and launch entries (so the second call runs over the first call's
-leftovers in the shared array), and checks each result against the regular
+This test calls the variant through the C ABI three times in a row, with
+different shapes and launch entries (32- and 64-key tiles; each call runs over
+the previous call's leftovers in the shared array), and checks each result against the regular
 entry point with a workspace, within the parity tolerance of the GPU tests.
 It also checks that a problem whose partials exceed the array is refused.
 The file is named so that pytest collects it last.
@@ -66,8 +66,9 @@ def test_no_alloc_matches_workspace_entry_point(cuda_lib):
     cases = [
         ((2, 2, 64, 8192, 2048), 20261103, _native.Launch(_native.FAMILY_WARP_MMA, 16, 32, 6)),
         ((1, 3, 32, 4096, 512), 20261102, _native.Launch(_native.FAMILY_AUTO, 0, 0, 0)),
+        ((1, 2, 32, 4096, 1024), 5, _native.Launch(_native.FAMILY_WARP_MMA, 16, 64, 4)),
     ]
-    for shape, seed, launch in cases:  # two calls in a row over the shared array
+    for shape, seed, launch in cases:  # calls in a row over the shared array
         data = [t.cuda() for t in oracle.make_inputs(shape, seed, "normal")]
         expected = _with_workspace(cuda_lib, data, launch)
         got = _no_alloc(cuda_lib, data, launch)
