@@ -237,13 +237,16 @@ def forward(q, kv, q_rope, k_rope, indices, *, config=None, cores=28, return_ker
 def _launch_records(launch, count):
     """Descriptors of the kernels one call enqueued, in launch order: the
     union build before the union launch's pair kernel; the split merge after
-    a main kernel with split > 1."""
+    a main kernel with split > 1, unless the main kernel merged its partials
+    itself (the split-V family's cluster merge: one kernel)."""
     name = "dsa_fwd_" + _FAMILY_NAMES.get(launch.family, str(launch.family))
     fields = (launch.family, launch.heads_per_cta, launch.keys_per_tile, launch.split)
     if launch.family == _native.FAMILY_PAIR_UNION:
         names = ["dsa_union_build", name]
+    elif launch.split > 1 and not (launch.family == _native.FAMILY_UMMA and count == 1):
+        names = [name, "dsa_merge"]
     else:
-        names = [name] + (["dsa_merge"] if launch.split > 1 else [])
+        names = [name]
     if len(names) != count:
         raise RuntimeError(f"library enqueued {count} kernels, expected {names}")
     return tuple(LaunchRecord(n, *fields) for n in names)

@@ -45,15 +45,29 @@ struct Layout {
   uint64_t num_off, max_off, sum_off, total;
 };
 
-Layout partial_layout(int64_t tokens, int64_t heads, int64_t split) {
+// Split partials (dsa/api.py:111-113): numerator [T, S, H, 512] FP32 and
+// max / sum [T, S, H] FP32. The umma family's cluster merge keeps the same
+// numerator and, instead of max / sum, (max, sum) pairs per value half
+// [T, 2, S, H] (each cluster merges one half on its own).
+Layout partial_layout(int64_t tokens, int64_t heads, int64_t split, bool cluster_merge = false) {
   Layout lay{0, 0, 0, 0};
   if (split <= 1) return lay;
   const uint64_t rows = (uint64_t)tokens * (uint64_t)split * (uint64_t)heads;
   lay.num_off = 0;
   lay.max_off = align_up(rows * dsa::kDimLatent * sizeof(float));
+  if (cluster_merge) {
+    lay.sum_off = lay.max_off;
+    lay.total = lay.max_off + align_up(rows * 2u * 2u * sizeof(float));
+    return lay;
+  }
   lay.sum_off = lay.max_off + align_up(rows * sizeof(float));
   lay.total = lay.sum_off + align_up(rows * sizeof(float));
   return lay;
+}
+
+// Whether a launch entry merges its split partials inside the main kernel.
+bool merges_in_kernel(const dsa_launch_t& e) {
+  return e.family == DSA_FAMILY_UMMA && e.split > 1 && dsa::umma_cluster_merge(e.split);
 }
 
 // Union launch: per block of 128 / H queries, up to (128 / H) * topk union
@@ -169,6 +183,9 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
     // at least two tiles per item: a one-tile item is all start-up (Q load,
     // first gather, epilogue) and doubles the partials the merge reads
     if (split > tiles / 2) split = tiles / 2;
+    // the split CTAs of a (token, value half) merge their partials as one
+    // cluster (at most 16 CTAs), all clusters resident at once if possible
+    if (split > 1) split = dsa::umma_cluster_split(halves, (int)split);
     if (split < 1) split = 1;
     e.split = (int32_t)split;
     *out = e;
@@ -216,7 +233,7 @@ uint64_t dsa_fwd_workspace_bytes(const dsa_fwd_args_t* a) {
   if (dsa_check_launch(a->batch, a->queries, a->heads, a->length, a->topk, &e) != DSA_STATUS_OK)
     return 0;
   if (e.family == DSA_FAMILY_PAIR_UNION) return union_layout(a->batch * a->queries, a->heads, a->topk).total;
-  return partial_layout(a->batch * a->queries, a->heads, e.split).total;
+  return partial_layout(a->batch * a->queries, a->heads, e.split, merges_in_kernel(e)).total;
 }
 
 int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
@@ -237,7 +254,8 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
   if (st != DSA_STATUS_OK) return st;
 
   const int64_t tokens = a->batch * a->queries;
-  const Layout lay = partial_layout(tokens, a->heads, e.split);
+  const bool fused_merge = merges_in_kernel(e);
+  const Layout lay = partial_layout(tokens, a->heads, e.split, fused_merge);
   if (e.family == DSA_FAMILY_PAIR_UNION) {
     const UnionLayout ul = union_layout(tokens, a->heads, a->topk);
     if (a->workspace == nullptr || a->workspace_bytes < ul.total ||
@@ -312,7 +330,7 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
   }
   if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;
   int launches = e.family == DSA_FAMILY_PAIR_UNION ? 2 : 1;  // union build + pair kernel
-  if (e.split > 1) {
+  if (e.split > 1 && !fused_merge) {
     err = dsa::launch_merge(p.part_num, p.part_max, p.part_sum, p.out, p.out_max, p.out_sum,
                             p.tokens, p.heads, p.split, s);
     if (err != cudaSuccess) return DSA_STATUS_LAUNCH_FAILED;

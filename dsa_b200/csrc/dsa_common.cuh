@@ -157,6 +157,12 @@ cudaError_t launch_fwd_warp_mma(const FwdParams& p, cudaStream_t stream);
 cudaError_t launch_fwd_umma(const FwdParams& p, cudaStream_t stream);
 // CTAs of the umma family that fit on the current device at once (-1 on error).
 int umma_max_ctas();
+// Whether the umma family merges `split` > 1 partials inside one launch
+// (clusters of `split` CTAs fit on the device; at most 16).
+bool umma_cluster_merge(int split);
+// Largest split <= `split` (and <= 16) whose clusters fit `clusters` at once
+// on the device; `split` capped at 16 when none does.
+int umma_cluster_split(long long clusters, int split);
 cudaError_t launch_fwd_pair(const FwdParams& p, cudaStream_t stream);
 // CTAs of the pair family (two per cluster) resident at once (-1 on error).
 int pair_max_ctas();

@@ -58,6 +58,7 @@ constexpr int kUmThreads = 32 * (kSoftWarp0 + kSoftWarps);  // 384
 constexpr int kUmHeads = 128;
 constexpr int kQTmemDims = 320;    // Q dims kept in TMEM (A operand of TS steps)
 constexpr int kQkSteps = kDimQK / 16;        // 36
+constexpr int kUmMaxClusterSplit = 16;       // largest cluster of the cluster-merge launch
 constexpr int kTsSteps = kQTmemDims / 16;    // 20
 
 // Shared-memory layout (bytes from a 1024-aligned base).
@@ -122,8 +123,8 @@ __device__ __forceinline__ Item make_item(const FwdParams& p, int item) {
   return it;
 }
 
-// Position of one tile in this CTA's sequence of tiles (items blockIdx.x,
-// blockIdx.x + gridDim.x, ...; tiles 0..ntiles-1 of each).
+// Position of one tile in this CTA's sequence of tiles (items first,
+// first + gridDim.x, ...; tiles 0..ntiles-1 of each).
 struct TileCursor {
   int item, t;
   Item w;
@@ -138,9 +139,9 @@ __device__ __forceinline__ void cursor_advance(const FwdParams& p, int n_items, 
   }
 }
 
-__device__ __forceinline__ TileCursor cursor_start(const FwdParams& p, int n_items, int k) {
+__device__ __forceinline__ TileCursor cursor_start(const FwdParams& p, int n_items, int first, int k) {
   TileCursor c;
-  c.item = blockIdx.x;
+  c.item = first;
   c.t = 0;
   if (c.item < n_items) c.w = make_item(p, c.item);
   cursor_advance(p, n_items, c, k);
@@ -163,6 +164,17 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// First work item of this CTA. Persistent launch: items blockIdx.x,
+// blockIdx.x + gridDim.x, ... Cluster-merge launch (one item per CTA): the
+// `split` CTAs of a cluster take the splits of one (token, value half).
+template <bool kCM>
+__device__ __forceinline__ int first_item(const FwdParams& p) {
+  if (!kCM) return (int)blockIdx.x;
+  const int c = (int)blockIdx.x / p.split;  // (token, half) of the cluster
+  const int sp = (int)blockIdx.x % p.split;
+  return (((c >> 1) * p.split + sp) << 1) | (c & 1);
 }
 
 // Bounded wait (limit_ns) whose result is the same in every lane of the warp.
@@ -215,6 +227,109 @@ __device__ __forceinline__ void store_o_part(const FwdParams& p, const Item& w, 
   }
 }
 
+// Epilogue of the cluster-merge launch, run by all 384 threads of every CTA
+// of the cluster (the two cluster barriers are always taken, also by a CTA
+// that gave up on a wait; it then skips the work). The CTA of split sp holds
+// O_sp (128 rows x 256 columns of its value half, relative to its running
+// max m_used) in TMEM and, per row, (m_sp, l, f) in shared memory, with
+// l relative to m_used and f = exp(m_used - m_sp). The merge of
+// dsa/merge.py:13-91 then is: M = max_s m_s, w_s = exp(m_s - M),
+// L = sum_s w_s l_s, O = sum_s (w_s f_s / L) O_s.
+//   1. each CTA writes its rows' (m_sp, l f) to the L2;  cluster barrier;
+//   2. each CTA reads every split's statistics of its rows, scales its O by
+//      w_sp f / L and writes it (FP32) to the L2; the owner of a row (half 0)
+//      writes softmax_max / softmax_sum;  cluster barrier;
+//   3. CTA rank r sums rows [128 r / S, 128 (r + 1) / S) over the S splits
+//      and writes them as BF16.
+// Statistics: [token][half][split][128] (m, l); partials: [token][split][128][512].
+__device__ __forceinline__ void merged_epilogue(const FwdParams& p, uint8_t* sbase, uint32_t tmem, bool live) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = p.split;
+  const int sp = (int)blockIdx.x % S;  // == %cluster_ctarank
+  const int cl = (int)blockIdx.x / S;
+  const int token = cl >> 1, half = cl & 1;
+  const float c = p.scale_log2;
+  float2* const pstat = reinterpret_cast<float2*>(p.part_max);
+  const float4* const srow = reinterpret_cast<const float4*>(sbase + kOffQ);
+  const int row = (warp & 3) * 32 + lane;  // the head row of warps 4..11
+  const int r0 = sp * kUmHeads / S, r1 = (sp + 1) * kUmHeads / S;
+  if (live && warp >= kSoftWarp0) {
+    const float4 st = srow[row];
+    pstat[((size_t)cl * S + sp) * kUmHeads + row] = make_float2(st.x, st.y * st.z);
+  }
+  cluster_sync();
+  if (live && warp >= kQkWarp0) {
+    tc_fence_after();
+    const float4 st = srow[row];
+    const float2* const rs = pstat + (size_t)cl * S * kUmHeads + row;
+    float2 ms[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < S) ms[k] = __ldcg(rs + (size_t)k * kUmHeads);
+    float M = kNegFltMax;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < S) M = fmaxf(M, ms[k].x);
+    float L = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < S && ms[k].y > 0.f) L += ms[k].y * ex2((ms[k].x - M) * c);
+    // an all-masked split (l = 0, O = 0) and a row without any valid index
+    // (L = 0: output 0) contribute nothing
+    const float factor = L > 0.f ? st.z * ex2((st.x - M) * c) / L : 0.f;
+    const bool lower = warp >= kSoftWarp0;  // columns 0..127 of the half, else 128..255
+    float* dst = p.part_num + (((size_t)token * S + sp) * kUmHeads + row) * kDimLatent + half * 256 + (lower ? 0 : 128);
+    const bool wide = (reinterpret_cast<uintptr_t>(p.part_num) & 31u) == 0;
+    const uint32_t o_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + kTmemO + (lower ? 0u : 128u);
+    uint32_t o[32];
+#pragma unroll 1
+    for (int cb = 0; cb < 128; cb += 32) {
+      tmem_ld32(o_lane + cb, o);
+      tmem_wait_ld();
+      store_f32_row32(dst + cb, o, factor, wide);
+    }
+    if (lower && half == 0 && row >= r0 && row < r1) {
+      const size_t orow = (size_t)token * kUmHeads + row;
+      p.out_max[orow] = final_max(M, L, p.scale_div);
+      p.out_sum[orow] = L;
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (live) {
+    // rows [r0, r1) x 256 columns of this half: 64 groups of four columns per row
+    const int groups = (r1 - r0) * 64;
+    const size_t sstride = (size_t)kUmHeads * kDimLatent / 4;  // float4s between splits
+    const float4* const src = reinterpret_cast<const float4*>(p.part_num) +
+                              (((size_t)token * S) * kUmHeads) * (kDimLatent / 4) + half * 64;
+#pragma unroll 1
+    for (int i = threadIdx.x; i < groups; i += kUmThreads) {
+      const int rr = r0 + i / 64, g4 = i % 64;
+      const float4* sp4 = src + (size_t)rr * (kDimLatent / 4) + g4;
+      float4 acc = __ldcg(sp4);
+#pragma unroll 4
+      for (int k = 1; k < S; ++k) {
+        const float4 v = __ldcg(sp4 + k * sstride);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      uint2 h;
+      h.x = pack_bf16x2(acc.x, acc.y);
+      h.y = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(p.out + ((size_t)token * kUmHeads + rr) * kDimLatent + half * 256 + g4 * 4) = h;
+    }
+  }
+}
+
+// kCM: the cluster-merge launch. The `split` CTAs of one (token, value half)
+// form a thread-block cluster and merge their partials themselves (row
+// statistics and partial O through the L2, two cluster barriers), so no
+// separate merge kernel runs; one item per CTA. Otherwise persistent CTAs
+// write FP32 partials for merge_kernel (split > 1) or the output (split 1).
+template <bool kCM>
 __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -225,6 +340,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sbase + kOffAbort);
   auto bar = [&](int i) -> uint32_t { return base + kOffBar + 8u * (uint32_t)i; };
   const unsigned long long lim = p.wait_limit_ns != 0 ? p.wait_limit_ns : kWaitLimitNs;
+  const int item0 = first_item<kCM>(p);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUmStages; ++s) {
@@ -284,7 +400,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     // lane -> (key quarter kq, 16-byte chunk j8): 4 rows x 128 contiguous bytes per instruction
     const int j8 = lane & 7;
     const int kq = lane >> 3;
-    TileCursor cur = cursor_start(p, n_items, (int)s);
+    TileCursor cur = cursor_start(p, n_items, item0, (int)s);
     TileCursor nx = cur;
     cursor_advance(p, n_items, nx, kUmStages);
     TileCursor nx2 = nx;
@@ -341,7 +457,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const uint32_t d = tmem + kTmemS + i * kUmBN;
     uint32_t g = 0, it = 0, n = 0;  // n: tiles this issuer ran
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+    for (int item = item0; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
       // Every issuer observes every item's Q (even without a tile in it) and
       // acknowledges, so no issuer can fall a barrier phase behind.
@@ -383,7 +499,9 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         __syncwarp();
         ++n;
       }
-      if (!ok || !(ok = epilogue_upper_half(w, it))) break;
+      if (!ok) break;
+      if (kCM) continue;  // the merged epilogue after the roles writes O
+      if (!(ok = epilogue_upper_half(w, it))) break;
       if (lane == 0) mbar_arrive(bar(kOFree));
     }
     if (!ok && lane == 0) report_error(p.status, kErrTimeout);
@@ -392,7 +510,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
     uint32_t g = 0, it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+    for (int item = item0; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
       const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
       for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
@@ -415,7 +533,9 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         }
         __syncwarp();
       }
-      if (!ok || !(ok = epilogue_upper_half(w, it))) break;
+      if (!ok) break;
+      if (kCM) continue;
+      if (!(ok = epilogue_upper_half(w, it))) break;
     }
     if (!ok && lane == 0) report_error(p.status, kErrTimeout);
   } else {
@@ -428,7 +548,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const uint32_t* const mask_all = reinterpret_cast<const uint32_t*>(sbase + kOffMask);
     uint32_t g = 0, it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+    for (int item = item0; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
       if (it == 0 && p.wait_test != 0 && blockIdx.x == 0) {
         // failure-path test: wait on a barrier that nothing arrives at, so the
@@ -567,6 +687,13 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       ok = wait_warp(bar(kPvDone0 + ((g - 1) & 1u)), ((g - 1) >> 1) & 1u, abort_flag, lim);
       if (!ok) break;
       const float f = (m_true == kNegFltMax) ? 1.f : ex2((m_used - m_true) * c);
+      if (kCM) {
+        // every QK and PV of the item is complete: the Q rows in shared
+        // memory are free and hold the row statistics for the merged epilogue
+        reinterpret_cast<float4*>(sbase + kOffQ)[row] = make_float4(m_true, l, f, 0.f);
+        tc_fence_before();
+        continue;
+      }
       epi[row] = make_float2(l, f);
       tc_fence_before();
       __syncwarp();
@@ -609,6 +736,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     tc_fence_before();
     __syncthreads();
   }
+  if constexpr (kCM) merged_epilogue(p, sbase, tmem, *abort_flag == 0);
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -620,11 +748,11 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
 int umma_max_ctas() {
   static int cached = -1;
   if (cached > 0) return cached;
-  if (cudaFuncSetAttribute(fwd_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(fwd_umma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)kSmemBytes) != cudaSuccess)
     return -1;
   int per_sm = 0, dev = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_umma_kernel, kUmThreads, kSmemBytes) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_umma_kernel<false>, kUmThreads, kSmemBytes) !=
           cudaSuccess ||
       per_sm <= 0)
     return -1;
@@ -635,13 +763,75 @@ int umma_max_ctas() {
   return cached;
 }
 
+namespace {
+
+// Cluster-merge launch of `split` CTAs per cluster (non-portable above 8).
+void cm_launch_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, int split, long long ctas,
+                      cudaStream_t stream) {
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = (unsigned)split;
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
+  *cfg = cudaLaunchConfig_t{};
+  cfg->gridDim = dim3((unsigned)ctas, 1, 1);
+  cfg->blockDim = dim3(kUmThreads, 1, 1);
+  cfg->dynamicSmemBytes = kSmemBytes;
+  cfg->stream = stream;
+  cfg->attrs = attr;
+  cfg->numAttrs = 1;
+}
+
+// Clusters of `split` CTAs resident at once (0 if none fits), cached per size.
+int cm_active_clusters(int split) {
+  static int cached[kUmMaxClusterSplit + 1];
+  static bool init = false;
+  if (!init) {
+    if (cudaFuncSetAttribute(fwd_umma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(fwd_umma_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      return 0;
+    for (int s = 0; s <= kUmMaxClusterSplit; ++s) cached[s] = -1;
+    init = true;
+  }
+  if (split < 2 || split > kUmMaxClusterSplit) return 0;
+  if (cached[split] < 0) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    cm_launch_config(&cfg, &attr, split, split, nullptr);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fwd_umma_kernel<true>, &cfg) != cudaSuccess) {
+      cudaGetLastError();  // clear the error an unsupported cluster size leaves behind
+      n = 0;
+    }
+    cached[split] = n;
+  }
+  return cached[split];
+}
+
+}  // namespace
+
+bool umma_cluster_merge(int split) { return cm_active_clusters(split) > 0; }
+
+int umma_cluster_split(long long clusters, int split) {
+  if (split > kUmMaxClusterSplit) split = kUmMaxClusterSplit;
+  for (int s = split; s >= 2; --s)
+    if (cm_active_clusters(s) >= clusters) return s;
+  return split;
+}
+
 cudaError_t launch_fwd_umma(const FwdParams& p, cudaStream_t stream) {
   if (p.heads != kUmHeads || p.keys_per_tile != kUmBN) return cudaErrorInvalidValue;
+  const long long items = (long long)p.tokens * p.split * 2;
+  if (p.split > 1 && umma_cluster_merge(p.split)) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    cm_launch_config(&cfg, &attr, p.split, items, stream);
+    return cudaLaunchKernelEx(&cfg, fwd_umma_kernel<true>, p);
+  }
   const int max_ctas = umma_max_ctas();
   if (max_ctas <= 0) return cudaErrorInvalidConfiguration;
-  const long long items = (long long)p.tokens * p.split * 2;
   const int ctas = (int)(items < max_ctas ? items : max_ctas);
-  fwd_umma_kernel<<<ctas, kUmThreads, kSmemBytes, stream>>>(p);
+  fwd_umma_kernel<false><<<ctas, kUmThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }
 
