@@ -616,8 +616,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
         float m_w = kNegFltMax;     // max used for this warp's latest tile
         float m_true = kNegFltMax;  // true max over this warp's tiles
         float l = 0.f;              // sum over this warp's tiles, relative to m_w
-        for (int t = 0; t < w.ntiles; ++t, ++g) {
-          if ((g & 1u) != e) continue;
+        const uint32_t g_item = g;
+        for (int t = (int)((e - g_item) & 1u); t < w.ntiles; t += 2) {
+          g = g_item + (uint32_t)t;
           if (t == max(w.ntiles - 8, 0) && quad == 0 && item + ncl < n_items && lane < 9) {
             // the next item's Q rows -> L2 (128 KB latent + 16 KB rope), so
             // that its load at the item boundary hits L2
@@ -629,12 +630,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           }
           const uint32_t i = g % kSBufs;
           // S complete (a non-blocking test first: it almost always is)
-          {
-            const bool rdy = lane == 0 ? mbar_test(bar(kSFull0 + i), (g / kSBufs) & 1u) : false;
-            if (__shfl_sync(0xffffffffu, rdy ? 1 : 0, 0) == 0 &&
-                !(ok = wait_warp(bar(kSFull0 + i), (g / kSBufs) & 1u, abort_flag)))
-              break;
-          }
+          if (!__all_sync(0xffffffffu, mbar_test(bar(kSFull0 + i), (g / kSBufs) & 1u)) &&
+              !(ok = wait_warp(bar(kSFull0 + i), (g / kSBufs) & 1u, abort_flag)))
+            break;
           // validity bits of the tile's keys, published by its gather warp
           // (written before the gather, so present once S is)
           uint32_t mbits, mtag;
@@ -718,7 +716,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           // staging slot ls (this warp's) is free once the bulk copy of
           // tile g - 4 has read it
           const uint32_t ls = g % kLSlots;
-          if (g >= kLSlots && !(ok = wait_warp(bar(kLFree0 + ls), ((g / kLSlots) - 1) & 1u, abort_flag))) break;
+          if (g >= kLSlots && !__all_sync(0xffffffffu, mbar_test(bar(kLFree0 + ls), ((g / kLSlots) - 1) & 1u)) &&
+              !(ok = wait_warp(bar(kLFree0 + ls), ((g / kLSlots) - 1) & 1u, abort_flag)))
+            break;
           uint8_t* const lslot = sbase + kOffLocal + ls * kSlotBytes;
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -730,6 +730,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(kLFull0 + ls));
         }
+        g = g_item + (uint32_t)w.ntiles;
         if (!ok) break;
         // ---- item end: combine the two warps' (max used, sum, true max) ----
         {

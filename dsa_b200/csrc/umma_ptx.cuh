@@ -121,7 +121,7 @@ __device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t
   if ((threadIdx.x & 31) == 0 && *word != value) {
     const unsigned long long start = global_ns();
     for (uint32_t k = 1; *word != value; ++k) {
-      if ((k & 15u) == 0) {
+      if ((k & 3u) == 0) {
         if (*abort) {
           ok = false;
           break;
@@ -131,8 +131,8 @@ __device__ __forceinline__ bool wait_word_warp(volatile uint32_t* word, uint32_t
           ok = false;
           break;
         }
-        __nanosleep(64);
       }
+      __nanosleep(32);
     }
   }
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
