@@ -41,7 +41,14 @@ EXPORTS = (
     "dsa_last_launch_count",
     "dsa_sparse_mla_fwd_noalloc",
     "dsa_set_wait_test",
+    "dsa_fwd_paged_workspace_bytes",
+    "dsa_sparse_mla_fwd_paged",
+    "dsa_fwd_fp8_workspace_bytes",
+    "dsa_sparse_mla_fwd_fp8",
 )
+
+# Bytes per token of the FP8 KV cache (DSA_FP8_ROW_BYTES in include/dsa_b200.h).
+FP8_ROW_BYTES = 656
 
 # Byte size of the built-in scratch array of dsa_sparse_mla_fwd_noalloc
 # (DSA_NOALLOC_SCRATCH_BYTES in include/dsa_b200.h).
@@ -51,6 +58,11 @@ NOALLOC_SCRATCH_BYTES = 32 << 20
 class Launch(ctypes.Structure):
     _fields_ = [("family", ctypes.c_int32), ("heads_per_cta", ctypes.c_int32),
                 ("keys_per_tile", ctypes.c_int32), ("split", ctypes.c_int32)]
+
+
+class PagedKv(ctypes.Structure):
+    _fields_ = [("block_table", ctypes.c_void_p), ("seq_lens", ctypes.c_void_p),
+                ("max_blocks", ctypes.c_int64), ("block_size", ctypes.c_int64), ("num_blocks", ctypes.c_int64)]
 
 
 class FwdArgs(ctypes.Structure):
@@ -100,6 +112,14 @@ def load():
         lib.dsa_last_launch_count.restype = ctypes.c_int
         lib.dsa_sparse_mla_fwd_noalloc.restype = ctypes.c_int
         lib.dsa_sparse_mla_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+        lib.dsa_fwd_paged_workspace_bytes.restype = ctypes.c_uint64
+        lib.dsa_fwd_paged_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(PagedKv)]
+        lib.dsa_sparse_mla_fwd_paged.restype = ctypes.c_int
+        lib.dsa_sparse_mla_fwd_paged.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(PagedKv), ctypes.c_void_p]
+        lib.dsa_fwd_fp8_workspace_bytes.restype = ctypes.c_uint64
+        lib.dsa_fwd_fp8_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
+        lib.dsa_sparse_mla_fwd_fp8.restype = ctypes.c_int
+        lib.dsa_sparse_mla_fwd_fp8.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
         lib.dsa_set_wait_test.restype = ctypes.c_int
         lib.dsa_set_wait_test.argtypes = [ctypes.c_uint64, ctypes.c_int]
         version = lib.dsa_abi_version()

@@ -252,6 +252,156 @@ def _launch_records(launch, count):
     return tuple(LaunchRecord(n, *fields) for n in names)
 
 
+def _check_paged(q, kv_cache, q_rope, k_rope_cache, block_table, indices, seq_lens):
+    """Contract of forward_paged: q/q_rope/indices as for forward; the caches
+    are page pools [NB, BS, 1, 512] / [NB, BS, 1, 64] BF16; block_table
+    [B, MB] int32; seq_lens [B] int32 or None; all contiguous on one CUDA
+    device."""
+    if len(q.shape) != 4 or len(indices.shape) != 4 or len(kv_cache.shape) != 4 or len(block_table.shape) != 2:
+        raise ValueError("q, kv_cache and indices must be 4-D tensors and block_table 2-D")
+    batch, queries, heads, width = q.shape
+    num_blocks, block_size = kv_cache.shape[0], kv_cache.shape[1]
+    topk = indices.shape[-1]
+    if (width != 512 or q_rope.shape != (batch, queries, heads, 64) or indices.shape != (batch, queries, 1, topk)
+            or kv_cache.shape != (num_blocks, block_size, 1, 512)
+            or k_rope_cache.shape != (num_blocks, block_size, 1, 64) or block_table.shape[0] != batch
+            or min(batch, queries, heads, topk, num_blocks, block_size, block_table.shape[1]) <= 0
+            or (seq_lens is not None and tuple(seq_lens.shape) != (batch,))):
+        raise ValueError("need q[B,SQ,H,512], q_rope[B,SQ,H,64], indices[B,SQ,1,K], kv_cache[NB,BS,1,512], "
+                         "k_rope_cache[NB,BS,1,64], block_table[B,MB], seq_lens[B]")
+    device = q.device
+    tensors = [q, kv_cache, q_rope, k_rope_cache, block_table, indices] + ([seq_lens] if seq_lens is not None else [])
+    if device.type != DEVICE_TYPE or any(t.device != device or not t.is_contiguous() for t in tensors):
+        raise ValueError("all inputs must be contiguous and on the same CUDA device")
+    bf16 = torch.bfloat16
+    if (q.dtype != bf16 or kv_cache.dtype != bf16 or q_rope.dtype != bf16 or k_rope_cache.dtype != bf16
+            or indices.dtype != torch.int32 or block_table.dtype != torch.int32
+            or (seq_lens is not None and seq_lens.dtype != torch.int32)):
+        raise ValueError("q/kv_cache/q_rope/k_rope_cache must be bfloat16; indices, block_table, seq_lens int32")
+    if num_blocks * block_size > 0x7fffffff:
+        raise ValueError("the page pool holds more than 2^31 - 1 rows")
+    return (batch, queries, heads, topk, num_blocks, block_size, block_table.shape[1]), device
+
+
+def forward_paged(q, kv_cache, q_rope, k_rope_cache, block_table, indices, *, seq_lens=None, config=None,
+                  cores=28, scale=None):
+    """``forward`` over a paged KV cache.
+
+    ``kv_cache`` / ``k_rope_cache`` are page pools ``[NB, BS, 1, 512]`` /
+    ``[NB, BS, 1, 64]``; ``block_table[b, j]`` is the pool block holding
+    tokens ``[j*BS, (j+1)*BS)`` of batch row ``b``; ``indices`` are logical
+    token positions. An index is masked when negative, at or past
+    ``seq_lens[b]`` (or ``MB * BS``), or when its table entry is outside
+    ``[0, NB)``. The result equals ``forward`` on the dense cache that the
+    table describes (same kernels, same arithmetic). The reference has no
+    paged layout (README.md:19-20); this is the adjacent KV-cache format.
+    """
+    (batch, queries, heads, topk, num_blocks, block_size, max_blocks), device = _check_paged(
+        q, kv_cache, q_rope, k_rope_cache, block_table, indices, seq_lens)
+    scale_arg = _check_scale(scale)
+    inner = (1, batch * queries, heads, num_blocks * block_size, topk)
+    if config is None:
+        _check_cores(cores)
+        launch = _default_launch(inner, device)
+    else:
+        _check_tuning(config, inner, cores)
+        launch = _launch_from_tuning(config, inner)
+    output = torch.empty_like(q)
+    maximum = torch.empty((batch, 1, queries, heads), device=device, dtype=torch.float32)
+    denominator = torch.empty_like(maximum)
+    args = _native.FwdArgs()
+    args.q, args.kv, args.q_rope, args.k_rope = q.data_ptr(), kv_cache.data_ptr(), q_rope.data_ptr(), k_rope_cache.data_ptr()
+    args.indices = indices.data_ptr()
+    args.output, args.softmax_max, args.softmax_sum = output.data_ptr(), maximum.data_ptr(), denominator.data_ptr()
+    args.batch, args.queries, args.heads, args.length, args.topk = batch, queries, heads, num_blocks * block_size, topk
+    args.launch = launch
+    args.scale = scale_arg
+    paged = _native.PagedKv(block_table.data_ptr(), seq_lens.data_ptr() if seq_lens is not None else None,
+                            max_blocks, block_size, num_blocks)
+    lib = _native.load()
+    ws_bytes = int(lib.dsa_fwd_paged_workspace_bytes(ctypes.byref(args), ctypes.byref(paged)))
+    if ws_bytes == 0:
+        raise ValueError(f"no launch entry for the paged shape {inner}")
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+    args.workspace, args.workspace_bytes = workspace.data_ptr(), ws_bytes
+    args.status = _status_word(device).data_ptr()
+    stream = torch.cuda.current_stream(device).cuda_stream if DEVICE_TYPE == "cuda" else 0
+    code = lib.dsa_sparse_mla_fwd_paged(ctypes.byref(args), ctypes.byref(paged), stream)
+    _native.raise_for_status(code, "dsa_sparse_mla_fwd_paged")
+    return output, maximum, denominator
+
+
+FP8_WORKSPACE_BUDGET = 1 << 30  # bytes of dequantised rows per dsa_sparse_mla_fwd_fp8 call
+
+
+def forward_fp8(q, kv_fp8, q_rope, indices, *, config=None, cores=28, scale=None):
+    """``forward`` over an FP8 KV cache (DeepSeek-V3.2's FP8 MLA layout).
+
+    ``kv_fp8`` is uint8 ``[B, L, 1, 656]`` per token: 512 float8 e4m3
+    latent values, 4 FP32 scales (one per 128 latent dims), 64 BF16 rope
+    dims (see ``quantize_kv_fp8``). Each query's selected rows are
+    dequantised (``bf16(e4m3 * scale)``) into a workspace by one kernel and
+    the BF16 forward runs on them, in pieces of whole queries that keep the
+    workspace under ``FP8_WORKSPACE_BUDGET``. The reference keeps kv in BF16
+    and leaves quantised caches out (DSA从原理到实现.md:626).
+    """
+    if len(q.shape) != 4 or len(kv_fp8.shape) != 4 or len(indices.shape) != 4:
+        raise ValueError("q, kv_fp8 and indices must be 4-D tensors")
+    batch, queries, heads, width = q.shape
+    length, topk = kv_fp8.shape[1], indices.shape[-1]
+    if (width != 512 or kv_fp8.shape != (batch, length, 1, _native.FP8_ROW_BYTES)
+            or q_rope.shape != (batch, queries, heads, 64) or indices.shape != (batch, queries, 1, topk)
+            or min(batch, queries, heads, length, topk) <= 0):
+        raise ValueError("need q[B,SQ,H,512], kv_fp8[B,L,1,656] uint8, q_rope[B,SQ,H,64], indices[B,SQ,1,K]")
+    device = q.device
+    if (device.type != DEVICE_TYPE or any(t.device != device or not t.is_contiguous()
+                                          for t in (q, kv_fp8, q_rope, indices))):
+        raise ValueError("all inputs must be contiguous and on the same CUDA device")
+    if (q.dtype != torch.bfloat16 or q_rope.dtype != torch.bfloat16 or kv_fp8.dtype != torch.uint8
+            or indices.dtype != torch.int32):
+        raise ValueError("q/q_rope must be bfloat16, kv_fp8 uint8 and indices int32")
+    scale_arg = _check_scale(scale)
+    if config is not None:
+        _check_tuning(config, (batch * queries, 1, heads, topk, topk), cores)
+    else:
+        _check_cores(cores)
+    output = torch.empty_like(q)
+    maximum = torch.empty((batch, 1, queries, heads), device=device, dtype=torch.float32)
+    denominator = torch.empty_like(maximum)
+    lib = _native.load()
+    stream = torch.cuda.current_stream(device).cuda_stream if DEVICE_TYPE == "cuda" else 0
+    per_query = topk * (1024 + 128 + 4)
+    chunk = max(1, min(queries, FP8_WORKSPACE_BUDGET // per_query))
+    rows_per_batch = length * _native.FP8_ROW_BYTES
+    for b in range(batch):
+        for s0 in range(0, queries, chunk):
+            n = min(chunk, queries - s0)
+            t0 = b * queries + s0
+            shape = (n, 1, heads, topk, topk)  # the inner forward's shape
+            launch = _launch_from_tuning(config, shape) if config is not None else _default_launch(shape, device)
+            args = _native.FwdArgs()
+            args.q = q.data_ptr() + t0 * heads * 512 * 2
+            args.q_rope = q_rope.data_ptr() + t0 * heads * 64 * 2
+            args.kv = kv_fp8.data_ptr() + b * rows_per_batch
+            args.k_rope = None
+            args.indices = indices.data_ptr() + t0 * topk * 4
+            args.output = output.data_ptr() + t0 * heads * 512 * 2
+            args.softmax_max = maximum.data_ptr() + t0 * heads * 4
+            args.softmax_sum = denominator.data_ptr() + t0 * heads * 4
+            args.batch, args.queries, args.heads, args.length, args.topk = 1, n, heads, length, topk
+            args.launch = launch
+            args.scale = scale_arg
+            ws_bytes = int(lib.dsa_fwd_fp8_workspace_bytes(ctypes.byref(args)))
+            if ws_bytes == 0:
+                raise ValueError(f"no launch entry for the FP8 shape {shape}")
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+            args.workspace, args.workspace_bytes = workspace.data_ptr(), ws_bytes
+            args.status = _status_word(device).data_ptr()
+            code = lib.dsa_sparse_mla_fwd_fp8(ctypes.byref(args), stream)
+            _native.raise_for_status(code, "dsa_sparse_mla_fwd_fp8")
+    return output, maximum, denominator
+
+
 class ForwardPlan:
     """``forward`` prepared once for fixed input tensors.
 

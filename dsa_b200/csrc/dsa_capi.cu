@@ -358,6 +358,124 @@ int dsa_merge_partials(const float* numerator, const float* partial_max, const f
 
 int dsa_last_launch_count(void) { return g_last_launch_count; }
 
+namespace {
+// Inner (flat-pool) forward arguments of a paged call; false when invalid.
+bool paged_inner(const dsa_fwd_args_t* a, const dsa_paged_kv_t* pg, dsa_fwd_args_t* inner, uint64_t* rows_bytes) {
+  if (a == nullptr || pg == nullptr || pg->block_table == nullptr) return false;
+  if (pg->max_blocks <= 0 || pg->block_size <= 0 || pg->num_blocks <= 0) return false;
+  if (pg->num_blocks * pg->block_size > 0x7fffffffLL || pg->max_blocks * pg->block_size > 0x7fffffffLL) return false;
+  if (!shape_ok(a->batch, a->queries, a->heads, 1, a->topk)) return false;
+  *inner = *a;
+  inner->batch = 1;
+  inner->queries = a->batch * a->queries;
+  inner->length = pg->num_blocks * pg->block_size;
+  *rows_bytes = align_up((uint64_t)a->batch * (uint64_t)a->queries * (uint64_t)a->topk * sizeof(int32_t));
+  return true;
+}
+}  // namespace
+
+uint64_t dsa_fwd_paged_workspace_bytes(const dsa_fwd_args_t* a, const dsa_paged_kv_t* pg) {
+  dsa_fwd_args_t inner;
+  uint64_t rows_bytes = 0;
+  if (!paged_inner(a, pg, &inner, &rows_bytes)) return 0;
+  dsa_launch_t e = inner.launch;
+  if (e.family == DSA_FAMILY_AUTO &&
+      dsa_default_launch(inner.batch, inner.queries, inner.heads, inner.length, inner.topk, &e) != DSA_STATUS_OK)
+    return 0;
+  if (dsa_check_launch(inner.batch, inner.queries, inner.heads, inner.length, inner.topk, &e) != DSA_STATUS_OK)
+    return 0;
+  inner.launch = e;
+  return rows_bytes + dsa_fwd_workspace_bytes(&inner);
+}
+
+int dsa_sparse_mla_fwd_paged(const dsa_fwd_args_t* a, const dsa_paged_kv_t* pg, void* stream) {
+  g_last_launch_count = 0;
+  dsa_fwd_args_t inner;
+  uint64_t rows_bytes = 0;
+  if (!paged_inner(a, pg, &inner, &rows_bytes) || a->indices == nullptr) return DSA_STATUS_BAD_ARGUMENT;
+  if (a->workspace == nullptr || a->workspace_bytes < rows_bytes ||
+      (reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0)
+    return DSA_STATUS_WORKSPACE_TOO_SMALL;
+  int32_t* rows = static_cast<int32_t*>(a->workspace);
+  inner.indices = rows;
+  inner.workspace = a->workspace_bytes > rows_bytes ? static_cast<char*>(a->workspace) + rows_bytes : nullptr;
+  inner.workspace_bytes = a->workspace_bytes - rows_bytes;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dsa::launch_paged_rows(a->indices, pg->block_table, pg->seq_lens, rows, a->batch * a->queries * a->topk,
+                             (int)(a->queries * a->topk), (int)pg->max_blocks, (int)pg->block_size,
+                             (int)pg->num_blocks, s) != cudaSuccess)
+    return DSA_STATUS_LAUNCH_FAILED;
+  const int st = dsa_sparse_mla_fwd(&inner, stream);
+  if (st != DSA_STATUS_OK) return st;
+  g_last_launch_count += 1;
+  return DSA_STATUS_OK;
+}
+
+namespace {
+// Inner (dequantised, compact) forward of an FP8 call: B*SQ batch rows of
+// one query each over its TOPK gathered rows.
+struct Fp8Layout {
+  uint64_t kv_off, kr_off, ids_off, fwd_off;
+};
+bool fp8_inner(const dsa_fwd_args_t* a, dsa_fwd_args_t* inner, Fp8Layout* lay) {
+  if (a == nullptr || !shape_ok(a->batch, a->queries, a->heads, a->length, a->topk)) return false;
+  const uint64_t rows = (uint64_t)a->batch * (uint64_t)a->queries * (uint64_t)a->topk;
+  if (rows > 0x7fffffffULL) return false;
+  *inner = *a;
+  inner->batch = a->batch * a->queries;
+  inner->queries = 1;
+  inner->length = a->topk;
+  lay->kv_off = 0;
+  lay->kr_off = align_up(rows * dsa::kDimLatent * 2u);
+  lay->ids_off = lay->kr_off + align_up(rows * dsa::kDimRope * 2u);
+  lay->fwd_off = lay->ids_off + align_up(rows * 4u);
+  return true;
+}
+}  // namespace
+
+uint64_t dsa_fwd_fp8_workspace_bytes(const dsa_fwd_args_t* a) {
+  dsa_fwd_args_t inner;
+  Fp8Layout lay;
+  if (!fp8_inner(a, &inner, &lay)) return 0;
+  dsa_launch_t e = inner.launch;
+  if (e.family == DSA_FAMILY_AUTO &&
+      dsa_default_launch(inner.batch, inner.queries, inner.heads, inner.length, inner.topk, &e) != DSA_STATUS_OK)
+    return 0;
+  if (dsa_check_launch(inner.batch, inner.queries, inner.heads, inner.length, inner.topk, &e) != DSA_STATUS_OK)
+    return 0;
+  inner.launch = e;
+  return lay.fwd_off + dsa_fwd_workspace_bytes(&inner);
+}
+
+int dsa_sparse_mla_fwd_fp8(const dsa_fwd_args_t* a, void* stream) {
+  g_last_launch_count = 0;
+  dsa_fwd_args_t inner;
+  Fp8Layout lay;
+  if (!fp8_inner(a, &inner, &lay) || a->kv == nullptr || a->indices == nullptr) return DSA_STATUS_BAD_ARGUMENT;
+  if (!aligned16(a->kv)) return DSA_STATUS_BAD_ARGUMENT;
+  if (a->workspace == nullptr || a->workspace_bytes < lay.fwd_off ||
+      (reinterpret_cast<uintptr_t>(a->workspace) & (kAlign - 1)) != 0)
+    return DSA_STATUS_WORKSPACE_TOO_SMALL;
+  char* ws = static_cast<char*>(a->workspace);
+  __nv_bfloat16* kv_c = reinterpret_cast<__nv_bfloat16*>(ws + lay.kv_off);
+  __nv_bfloat16* kr_c = reinterpret_cast<__nv_bfloat16*>(ws + lay.kr_off);
+  int32_t* ids_c = reinterpret_cast<int32_t*>(ws + lay.ids_off);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dsa::launch_fp8_gather(static_cast<const uint8_t*>(a->kv), a->indices, kv_c, kr_c, ids_c,
+                             a->batch * a->queries * a->topk, (int)a->topk, (int)a->queries, (int)a->length,
+                             s) != cudaSuccess)
+    return DSA_STATUS_LAUNCH_FAILED;
+  inner.kv = kv_c;
+  inner.k_rope = kr_c;
+  inner.indices = ids_c;
+  inner.workspace = a->workspace_bytes > lay.fwd_off ? ws + lay.fwd_off : nullptr;
+  inner.workspace_bytes = a->workspace_bytes - lay.fwd_off;
+  const int st = dsa_sparse_mla_fwd(&inner, stream);
+  if (st != DSA_STATUS_OK) return st;
+  g_last_launch_count += 1;
+  return DSA_STATUS_OK;
+}
+
 int dsa_set_wait_test(uint64_t limit_ns, int stall) {
   g_wait_limit_ns.store((unsigned long long)limit_ns, std::memory_order_relaxed);
   g_wait_test.store(stall != 0 ? 1 : 0, std::memory_order_relaxed);

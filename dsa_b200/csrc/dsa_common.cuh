@@ -174,6 +174,12 @@ cudaError_t launch_union_build(const int32_t* ids, int topk, int length, int qpb
 // CTAs of the stream family resident at once (-1 on error).
 int stream_max_ctas();
 int keys_max_ctas();
+cudaError_t launch_paged_rows(const int32_t* ids, const int32_t* block_table, const int32_t* seq_lens, int32_t* rows,
+                              long long n, int per_batch, int max_blocks, int block_size, int num_blocks,
+                              cudaStream_t stream);
+cudaError_t launch_fp8_gather(const uint8_t* cache, const int32_t* ids, __nv_bfloat16* kv_out, __nv_bfloat16* kr_out,
+                              int32_t* ids_out, long long rows, int topk, int queries, int length,
+                              cudaStream_t stream);
 cudaError_t launch_merge(const float* num, const float* pmax, const float* psum,
                          __nv_bfloat16* out, float* omax, float* osum, int tokens, int heads,
                          int split, cudaStream_t stream);

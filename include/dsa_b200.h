@@ -155,6 +155,52 @@ DSA_B200_API int dsa_merge_partials(const float* numerator, const float* partial
                        float* softmax_sum, int64_t tokens, int64_t heads, int64_t split,
                        void* stream);
 
+/* Paged KV cache of a forward call (no counterpart in the reference, which
+ * reads a dense kv per batch row and lists paged caches as out of scope,
+ * README.md:19-20). args->kv / args->k_rope then point at page pools
+ * [num_blocks, block_size, 1, 512] / [num_blocks, block_size, 1, 64] BF16;
+ * block_table[b * max_blocks + j] is the pool block holding tokens
+ * [j * block_size, (j + 1) * block_size) of batch row b; args->indices are
+ * logical token positions of each batch row. An index is masked when it is
+ * negative, at or past seq_lens[b] (or max_blocks * block_size when
+ * seq_lens is NULL), or when its block table entry is outside
+ * [0, num_blocks). args->length is ignored. */
+typedef struct dsa_paged_kv {
+  const int32_t* block_table;  /* INT32 [B, max_blocks] */
+  const int32_t* seq_lens;     /* INT32 [B], or NULL */
+  int64_t max_blocks;
+  int64_t block_size;
+  int64_t num_blocks;
+} dsa_paged_kv_t;
+
+/* Workspace bytes of dsa_sparse_mla_fwd_paged: the translated row indices
+ * plus the forward's own workspace. 0 for invalid arguments. */
+DSA_B200_API uint64_t dsa_fwd_paged_workspace_bytes(const dsa_fwd_args_t* args, const dsa_paged_kv_t* paged);
+
+/* Forward over a paged KV cache: one kernel maps every logical index to its
+ * pool row, then the forward runs over the pool as one batch row of
+ * num_blocks * block_size rows (same kernels, same arithmetic as the dense
+ * call on the same logical data). Returns a dsa_status_t. */
+DSA_B200_API int dsa_sparse_mla_fwd_paged(const dsa_fwd_args_t* args, const dsa_paged_kv_t* paged, void* stream);
+
+/* Bytes per token of the FP8 KV cache of dsa_sparse_mla_fwd_fp8:
+ * 512 float8 e4m3 latent values, 4 FP32 scales (one per 128 latent dims),
+ * 64 BF16 rope dims (DeepSeek-V3.2's FP8 MLA cache layout). */
+#define DSA_FP8_ROW_BYTES 656
+
+/* Workspace bytes of dsa_sparse_mla_fwd_fp8 (the dequantised selected rows
+ * of every query plus the forward's own workspace); 0 for invalid arguments. */
+DSA_B200_API uint64_t dsa_fwd_fp8_workspace_bytes(const dsa_fwd_args_t* args);
+
+/* Forward over an FP8 KV cache (no counterpart in the reference, whose kv
+ * is BF16 and which lists quantised caches as out of scope,
+ * DSA从原理到实现.md:626). args->kv points at the cache, uint8
+ * [B, L, 1, DSA_FP8_ROW_BYTES]; args->k_rope is ignored. One kernel
+ * gathers each query's selected rows and dequantises them
+ * (latent = bf16(e4m3 * scale)) into the workspace; the BF16 forward then
+ * runs on them as B*SQ batch rows of TOPK keys. Returns a dsa_status_t. */
+DSA_B200_API int dsa_sparse_mla_fwd_fp8(const dsa_fwd_args_t* args, void* stream);
+
 /* Number of kernels the last successful dsa_sparse_mla_fwd on this host
  * thread enqueued (1 or 2), for launch accounting. Calls of
  * dsa_sparse_mla_fwd_noalloc do not update it. */

@@ -270,6 +270,53 @@ def passes(metrics: Dict[str, dict], gates: Dict[str, float] = GATES,
             and all(metrics[k]["max_relative"] <= g for k, g in element_gates.items()))
 
 
+def paged_to_dense(kv_cache, k_rope_cache, block_table, indices, seq_lens=None):
+    """Dense restatement of a paged KV cache (the paged format this build
+    adds; the reference has none, README.md:19-20).
+
+    ``block_table[b, j]`` is the pool block of tokens ``[j*BS, (j+1)*BS)`` of
+    batch row ``b``. Returns (kv [B, MB*BS, 1, 512], k_rope [B, MB*BS, 1, 64],
+    indices) where an index is set to -1 when negative, at or past
+    ``seq_lens[b]`` (or ``MB*BS``), or when its table entry is outside
+    ``[0, NB)``; the dense rows of such entries are zero.
+    """
+    num_blocks, block_size = kv_cache.shape[0], kv_cache.shape[1]
+    batch, max_blocks = block_table.shape
+    length = max_blocks * block_size
+    kv = torch.zeros((batch, length, 1, D_LATENT), dtype=kv_cache.dtype)
+    kr = torch.zeros((batch, length, 1, D_ROPE), dtype=k_rope_cache.dtype)
+    table_ok = torch.zeros((batch, max_blocks), dtype=torch.bool)
+    for b in range(batch):
+        for j in range(max_blocks):
+            blk = int(block_table[b, j])
+            if 0 <= blk < num_blocks:
+                kv[b, j * block_size:(j + 1) * block_size] = kv_cache[blk]
+                kr[b, j * block_size:(j + 1) * block_size] = k_rope_cache[blk]
+                table_ok[b, j] = True
+    ids = indices.clone().long()
+    limit = (seq_lens.long() if seq_lens is not None else torch.full((batch,), length)).reshape(batch, 1, 1, 1)
+    valid = (ids >= 0) & (ids < limit) & (ids < length)
+    blk_ok = table_ok.gather(1, ids.clamp(0, length - 1).reshape(batch, -1) // block_size).reshape(ids.shape)
+    valid &= blk_ok
+    ids[~valid] = -1
+    return kv, kr, ids.int()
+
+
+def dequantize_kv_fp8(cache):
+    """BF16 (kv, k_rope) of an FP8 KV cache uint8 ``[B, L, 1, 656]`` (the FP8
+    format this build adds, DeepSeek-V3.2's FP8 MLA layout; the reference has
+    none, DSA从原理到实现.md:626): bytes 0..511 float8 e4m3 latent values,
+    512..527 four FP32 scales (one per 128 latent dims), 528..655 the 64
+    rope dims as BF16; latent = bf16(float(e4m3) * scale)."""
+    lead = cache.shape[:-1]
+    raw = cache.reshape(-1, 656)
+    lat = raw[:, :512].contiguous().view(torch.float8_e4m3fn).float().reshape(-1, 4, 128)
+    scale = raw[:, 512:528].contiguous().view(torch.float32).reshape(-1, 4, 1)
+    kv = (lat * scale).reshape(*lead, 512).bfloat16()
+    kr = raw[:, 528:].contiguous().view(torch.bfloat16).reshape(*lead, 64)
+    return kv, kr
+
+
 def merge_partials(numerator, partial_max, partial_sum):
     """FP32 split-KV merge of dsa/merge.py:13-91 (restated in torch).
 
