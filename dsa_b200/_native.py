@@ -45,6 +45,8 @@ EXPORTS = (
     "dsa_sparse_mla_fwd_paged",
     "dsa_fwd_fp8_workspace_bytes",
     "dsa_sparse_mla_fwd_fp8",
+    "dsa_indexer_workspace_bytes",
+    "dsa_indexer_topk",
 )
 
 # Bytes per token of the FP8 KV cache (DSA_FP8_ROW_BYTES in include/dsa_b200.h).
@@ -63,6 +65,16 @@ class Launch(ctypes.Structure):
 class PagedKv(ctypes.Structure):
     _fields_ = [("block_table", ctypes.c_void_p), ("seq_lens", ctypes.c_void_p),
                 ("max_blocks", ctypes.c_int64), ("block_size", ctypes.c_int64), ("num_blocks", ctypes.c_int64)]
+
+
+class IndexerArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("weights", ctypes.c_void_p), ("lengths", ctypes.c_void_p),
+        ("indices", ctypes.c_void_p), ("scores", ctypes.c_void_p),
+        ("batch", ctypes.c_int64), ("queries", ctypes.c_int64), ("heads", ctypes.c_int64),
+        ("length", ctypes.c_int64), ("topk", ctypes.c_int64),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64), ("status", ctypes.c_void_p),
+    ]
 
 
 class FwdArgs(ctypes.Structure):
@@ -120,6 +132,10 @@ def load():
         lib.dsa_fwd_fp8_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
         lib.dsa_sparse_mla_fwd_fp8.restype = ctypes.c_int
         lib.dsa_sparse_mla_fwd_fp8.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+        lib.dsa_indexer_workspace_bytes.restype = ctypes.c_uint64
+        lib.dsa_indexer_workspace_bytes.argtypes = [ctypes.POINTER(IndexerArgs)]
+        lib.dsa_indexer_topk.restype = ctypes.c_int
+        lib.dsa_indexer_topk.argtypes = [ctypes.POINTER(IndexerArgs), ctypes.c_void_p]
         lib.dsa_set_wait_test.restype = ctypes.c_int
         lib.dsa_set_wait_test.argtypes = [ctypes.c_uint64, ctypes.c_int]
         version = lib.dsa_abi_version()

@@ -476,6 +476,41 @@ int dsa_sparse_mla_fwd_fp8(const dsa_fwd_args_t* a, void* stream) {
   return DSA_STATUS_OK;
 }
 
+namespace {
+bool indexer_ok(const dsa_indexer_args_t* a) {
+  if (a == nullptr) return false;
+  if (a->batch <= 0 || a->queries <= 0 || a->length <= 0 || a->topk <= 0) return false;
+  if (a->heads != 16 && a->heads != 32 && a->heads != 64 && a->heads != 128) return false;
+  if (a->batch * a->queries > 0x7fffffffLL || a->length > 0x7fffffffLL || a->topk > 0x7fffffffLL) return false;
+  return true;
+}
+}  // namespace
+
+uint64_t dsa_indexer_workspace_bytes(const dsa_indexer_args_t* a) {
+  if (!indexer_ok(a) || a->scores != nullptr) return 0;
+  return align_up((uint64_t)a->batch * (uint64_t)a->queries * (uint64_t)a->length * sizeof(float));
+}
+
+int dsa_indexer_topk(const dsa_indexer_args_t* a, void* stream) {
+  if (!indexer_ok(a) || !a->q || !a->k || !a->weights || !a->indices) return DSA_STATUS_BAD_ARGUMENT;
+  if (!aligned16(a->q) || !aligned16(a->k)) return DSA_STATUS_BAD_ARGUMENT;
+  float* scores = a->scores;
+  if (scores == nullptr) {
+    if (a->workspace == nullptr || a->workspace_bytes < dsa_indexer_workspace_bytes(a))
+      return DSA_STATUS_WORKSPACE_TOO_SMALL;
+    scores = static_cast<float*>(a->workspace);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dsa::launch_indexer_logits(static_cast<const __nv_bfloat16*>(a->q), static_cast<const __nv_bfloat16*>(a->k),
+                                 a->weights, a->lengths, scores, a->status, (int)a->batch, (int)a->queries,
+                                 (int)a->heads, (int)a->length, s) != cudaSuccess)
+    return DSA_STATUS_LAUNCH_FAILED;
+  if (dsa::launch_topk(scores, a->lengths, a->indices, a->batch * a->queries, (int)a->length, (int)a->topk, s) !=
+      cudaSuccess)
+    return DSA_STATUS_LAUNCH_FAILED;
+  return DSA_STATUS_OK;
+}
+
 int dsa_set_wait_test(uint64_t limit_ns, int stall) {
   g_wait_limit_ns.store((unsigned long long)limit_ns, std::memory_order_relaxed);
   g_wait_test.store(stall != 0 ? 1 : 0, std::memory_order_relaxed);

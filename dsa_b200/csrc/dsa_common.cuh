@@ -180,6 +180,11 @@ cudaError_t launch_paged_rows(const int32_t* ids, const int32_t* block_table, co
 cudaError_t launch_fp8_gather(const uint8_t* cache, const int32_t* ids, __nv_bfloat16* kv_out, __nv_bfloat16* kr_out,
                               int32_t* ids_out, long long rows, int topk, int queries, int length,
                               cudaStream_t stream);
+cudaError_t launch_indexer_logits(const __nv_bfloat16* q, const __nv_bfloat16* k, const float* w, const int32_t* lens,
+                                  float* scores, int32_t* status, int batch, int queries, int heads, int length,
+                                  cudaStream_t stream);
+cudaError_t launch_topk(const float* scores, const int32_t* lens, int32_t* out, long long rows, int length, int topk,
+                        cudaStream_t stream);
 cudaError_t launch_merge(const float* num, const float* pmax, const float* psum,
                          __nv_bfloat16* out, float* omax, float* osum, int tokens, int heads,
                          int split, cudaStream_t stream);

@@ -201,6 +201,34 @@ DSA_B200_API uint64_t dsa_fwd_fp8_workspace_bytes(const dsa_fwd_args_t* args);
  * runs on them as B*SQ batch rows of TOPK keys. Returns a dsa_status_t. */
 DSA_B200_API int dsa_sparse_mla_fwd_fp8(const dsa_fwd_args_t* args, void* stream);
 
+/* Lightning indexer + top-k: the stage that produces the indices of the
+ * forward (no counterpart in the reference, which takes the indices as
+ * given and leaves the indexer and top-k out, README.md:19-20). For every
+ * query t of batch row b and key j < L:
+ *   score[t][j] = sum_h weights[t][h] * relu(q[t][h] . k[b][j])
+ * (FP32, tcgen05 BF16 products), and indices[t] = the TOPK keys
+ * j < lengths[t] (or L) with the largest scores, ties to the smaller key,
+ * in ascending key order, padded with -1 when fewer keys are valid. */
+typedef struct dsa_indexer_args {
+  const void* q;            /* BF16 [B, SQ, HI, 128], HI in {16, 32, 64, 128} */
+  const void* k;            /* BF16 [B, L, 128] */
+  const float* weights;     /* FP32 [B, SQ, HI] */
+  const int32_t* lengths;   /* INT32 [B, SQ] valid keys per query, or NULL (all L) */
+  int32_t* indices;         /* INT32 [B, SQ, 1, TOPK] (output) */
+  float* scores;            /* FP32 [B, SQ, L] (output), or NULL: kept in the workspace */
+  int64_t batch, queries, heads, length, topk;
+  void* workspace;          /* scores when `scores` is NULL */
+  uint64_t workspace_bytes;
+  int32_t* status;          /* optional device word (bounded-wait timeouts) */
+} dsa_indexer_args_t;
+
+/* Workspace bytes of dsa_indexer_topk (B*SQ*L FP32 scores when the caller
+ * does not take them; 0 otherwise or for invalid arguments). */
+DSA_B200_API uint64_t dsa_indexer_workspace_bytes(const dsa_indexer_args_t* args);
+
+/* Indexer scores then top-k, two kernels on `stream`. Returns a dsa_status_t. */
+DSA_B200_API int dsa_indexer_topk(const dsa_indexer_args_t* args, void* stream);
+
 /* Number of kernels the last successful dsa_sparse_mla_fwd on this host
  * thread enqueued (1 or 2), for launch accounting. Calls of
  * dsa_sparse_mla_fwd_noalloc do not update it. */

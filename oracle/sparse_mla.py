@@ -317,6 +317,34 @@ def dequantize_kv_fp8(cache):
     return kv, kr
 
 
+def indexer_scores(q_idx, k_idx, weights):
+    """FP32 lightning-indexer scores (DeepSeek-V3.2's indexer; the reference
+    has none, README.md:19-20): ``score[b, s, j] = sum_h w[b, s, h] *
+    relu(q_idx[b, s, h] . k_idx[b, j])`` -> ``[B, SQ, L]``."""
+    prev = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+    try:
+        logits = torch.einsum("bshd,bld->bshl", q_idx.float(), k_idx.float())
+        return (weights.float()[..., None] * logits.clamp_min(0)).sum(2)
+    finally:
+        torch.set_float32_matmul_precision(prev)
+
+
+def topk_indices(scores, topk, lengths=None):
+    """The ``topk`` keys with the largest scores per query among keys
+    ``j < lengths[b, s]`` (or all), ties to the smaller key, ascending key
+    order, padded with -1 -> int32 ``[B, SQ, 1, topk]``."""
+    batch, queries, length = scores.shape
+    out = torch.full((batch, queries, 1, topk), -1, dtype=torch.int32)
+    for b in range(batch):
+        for s in range(queries):
+            n = length if lengths is None else max(0, min(int(lengths[b, s]), length))
+            order = torch.sort(-scores[b, s, :n], stable=True).indices[:topk]
+            sel = torch.sort(order).values
+            out[b, s, 0, :len(sel)] = sel.int()
+    return out
+
+
 def merge_partials(numerator, partial_max, partial_sum):
     """FP32 split-KV merge of dsa/merge.py:13-91 (restated in torch).
 
