@@ -107,42 +107,58 @@ def load():
             raise RuntimeError(
                 f"{LIB_PATH} is missing: build the sm_100a library first "
                 "(python -m dsa_b200.build or __graft_entry__.build()); there is no fallback")
-        lib = ctypes.CDLL(LIB_PATH)
-        lib.dsa_abi_version.restype = ctypes.c_int
-        lib.dsa_status_string.restype = ctypes.c_char_p
-        lib.dsa_status_string.argtypes = [ctypes.c_int]
-        lib.dsa_default_launch.restype = ctypes.c_int
-        lib.dsa_default_launch.argtypes = [ctypes.c_int64] * 5 + [ctypes.POINTER(Launch)]
-        lib.dsa_check_launch.restype = ctypes.c_int
-        lib.dsa_check_launch.argtypes = [ctypes.c_int64] * 5 + [ctypes.POINTER(Launch)]
-        lib.dsa_fwd_workspace_bytes.restype = ctypes.c_uint64
-        lib.dsa_fwd_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
-        lib.dsa_sparse_mla_fwd.restype = ctypes.c_int
-        lib.dsa_sparse_mla_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
-        lib.dsa_merge_partials.restype = ctypes.c_int
-        lib.dsa_merge_partials.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
-        lib.dsa_last_launch_count.restype = ctypes.c_int
-        lib.dsa_sparse_mla_fwd_noalloc.restype = ctypes.c_int
-        lib.dsa_sparse_mla_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
-        lib.dsa_fwd_paged_workspace_bytes.restype = ctypes.c_uint64
-        lib.dsa_fwd_paged_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(PagedKv)]
-        lib.dsa_sparse_mla_fwd_paged.restype = ctypes.c_int
-        lib.dsa_sparse_mla_fwd_paged.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(PagedKv), ctypes.c_void_p]
-        lib.dsa_fwd_fp8_workspace_bytes.restype = ctypes.c_uint64
-        lib.dsa_fwd_fp8_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
-        lib.dsa_sparse_mla_fwd_fp8.restype = ctypes.c_int
-        lib.dsa_sparse_mla_fwd_fp8.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
-        lib.dsa_indexer_workspace_bytes.restype = ctypes.c_uint64
-        lib.dsa_indexer_workspace_bytes.argtypes = [ctypes.POINTER(IndexerArgs)]
-        lib.dsa_indexer_topk.restype = ctypes.c_int
-        lib.dsa_indexer_topk.argtypes = [ctypes.POINTER(IndexerArgs), ctypes.c_void_p]
-        lib.dsa_set_wait_test.restype = ctypes.c_int
-        lib.dsa_set_wait_test.argtypes = [ctypes.c_uint64, ctypes.c_int]
+        lib = _bind(ctypes.CDLL(LIB_PATH))
         version = lib.dsa_abi_version()
         if version != ABI_VERSION:
             raise RuntimeError(f"libdsa_b200.so ABI {version} != expected {ABI_VERSION}; rebuild it")
         _lib = lib
         return lib
+
+
+CHECKED_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libdsa_b200_checked.so")
+
+
+def load_checked():
+    """The bounds-checking debug build (same ABI; a failed check sets bit 4 of
+    the status word). Raises RuntimeError when it has not been built."""
+    if not os.path.exists(CHECKED_LIB_PATH):
+        raise RuntimeError(f"{CHECKED_LIB_PATH} is missing: python -m dsa_b200.build --bounds-check")
+    return _bind(ctypes.CDLL(CHECKED_LIB_PATH))
+
+
+def _bind(lib):
+    """Declare the prototypes of include/dsa_b200.h on a loaded library."""
+    lib.dsa_abi_version.restype = ctypes.c_int
+    lib.dsa_status_string.restype = ctypes.c_char_p
+    lib.dsa_status_string.argtypes = [ctypes.c_int]
+    lib.dsa_default_launch.restype = ctypes.c_int
+    lib.dsa_default_launch.argtypes = [ctypes.c_int64] * 5 + [ctypes.POINTER(Launch)]
+    lib.dsa_check_launch.restype = ctypes.c_int
+    lib.dsa_check_launch.argtypes = [ctypes.c_int64] * 5 + [ctypes.POINTER(Launch)]
+    lib.dsa_fwd_workspace_bytes.restype = ctypes.c_uint64
+    lib.dsa_fwd_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
+    lib.dsa_sparse_mla_fwd.restype = ctypes.c_int
+    lib.dsa_sparse_mla_fwd.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+    lib.dsa_merge_partials.restype = ctypes.c_int
+    lib.dsa_merge_partials.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
+    lib.dsa_last_launch_count.restype = ctypes.c_int
+    lib.dsa_sparse_mla_fwd_noalloc.restype = ctypes.c_int
+    lib.dsa_sparse_mla_fwd_noalloc.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+    lib.dsa_fwd_paged_workspace_bytes.restype = ctypes.c_uint64
+    lib.dsa_fwd_paged_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(PagedKv)]
+    lib.dsa_sparse_mla_fwd_paged.restype = ctypes.c_int
+    lib.dsa_sparse_mla_fwd_paged.argtypes = [ctypes.POINTER(FwdArgs), ctypes.POINTER(PagedKv), ctypes.c_void_p]
+    lib.dsa_fwd_fp8_workspace_bytes.restype = ctypes.c_uint64
+    lib.dsa_fwd_fp8_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
+    lib.dsa_sparse_mla_fwd_fp8.restype = ctypes.c_int
+    lib.dsa_sparse_mla_fwd_fp8.argtypes = [ctypes.POINTER(FwdArgs), ctypes.c_void_p]
+    lib.dsa_indexer_workspace_bytes.restype = ctypes.c_uint64
+    lib.dsa_indexer_workspace_bytes.argtypes = [ctypes.POINTER(IndexerArgs)]
+    lib.dsa_indexer_topk.restype = ctypes.c_int
+    lib.dsa_indexer_topk.argtypes = [ctypes.POINTER(IndexerArgs), ctypes.c_void_p]
+    lib.dsa_set_wait_test.restype = ctypes.c_int
+    lib.dsa_set_wait_test.argtypes = [ctypes.c_uint64, ctypes.c_int]
+    return lib
 
 
 def status_string(code: int) -> str:

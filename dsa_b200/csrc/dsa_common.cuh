@@ -25,6 +25,19 @@ constexpr float kNegFltMax = -3.4028234663852886e38f;
 // Device error bits OR-ed into the optional status word.
 constexpr int kErrTimeout = 1;
 constexpr int kErrBadLaunch = 2;
+constexpr int kErrBounds = 4;  // a check of the bounds-checking build failed
+
+// The bounds-checking build (-DDSA_BOUNDS_CHECK, libdsa_b200_checked.so)
+// checks every gathered row index, batch row, shared-memory stage
+// destination and tensor-memory column it uses; a failed check ORs
+// kErrBounds into the status word and redirects the access to a safe
+// address (row 0, the stage's first byte, column 0) instead of trapping.
+// In the regular build the checks compile to nothing.
+#ifdef DSA_BOUNDS_CHECK
+constexpr bool kBoundsCheck = true;
+#else
+constexpr bool kBoundsCheck = false;
+#endif
 
 struct FwdParams {
   const __nv_bfloat16* q;
@@ -150,6 +163,36 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __device__ __forceinline__ void report_error(int32_t* status, int bits) {
   if (status != nullptr) atomicOr(status, bits);
+}
+
+// Bounds-checking build: `v` inside [0, n), else kErrBounds and 0.
+__device__ __forceinline__ int checked_index(int v, int n, int32_t* status) {
+  if (kBoundsCheck && (v < 0 || v >= n)) {
+    report_error(status, kErrBounds);
+    return 0;
+  }
+  return v;
+}
+// Bounds-checking build: a shared-memory destination of `bytes` inside
+// [lo, lo + size), else kErrBounds and lo.
+__device__ __forceinline__ uint32_t checked_smem(uint32_t addr, uint32_t bytes, uint32_t lo, uint32_t size,
+                                                 int32_t* status) {
+  if (kBoundsCheck && (addr < lo || addr + bytes > lo + size)) {
+    report_error(status, kErrBounds);
+    return lo;
+  }
+  return addr;
+}
+// Bounds-checking build: `ncols` tensor-memory columns from `col` inside
+// the allocation's `cols` columns (column = low 16 bits of the address),
+// else kErrBounds and column 0 of the same lane.
+__device__ __forceinline__ uint32_t checked_tmem(uint32_t taddr, uint32_t tbase, uint32_t ncols, uint32_t cols,
+                                                 int32_t* status) {
+  if (kBoundsCheck && ((taddr & 0xFFFFu) < (tbase & 0xFFFFu) || (taddr & 0xFFFFu) + ncols > (tbase & 0xFFFFu) + cols)) {
+    report_error(status, kErrBounds);
+    return (taddr & 0xFFFF0000u) | (tbase & 0xFFFFu);
+  }
+  return taddr;
 }
 
 // Launchers (each returns a cudaError_t from the launch).

@@ -232,17 +232,19 @@ __global__ void __launch_bounds__(kKyThreads, 1) fwd_keys_kernel(const FwdParams
     bool ok = true;
     while (cur.item < n_items) {
       if (n > 0 && !(ok = ky_wait(bar(kyEmpty0 + s), (n - 1) & 1u, abort_flag))) break;
-      const int row = min(max(idx_cur, 0), L - 1);  // clamped address; masked by the softmax
+      const int row = checked_index(min(max(idx_cur, 0), L - 1), L, p.status);  // clamped; masked by the softmax
       const uint32_t bits = __ballot_sync(0xffffffffu, (idx_cur >= 0) & (idx_cur < L));
       if (lane == 0) mask[2 * s + hf] = bits;
-      const __nv_bfloat16* const kv_b = p.kv + (size_t)cur.w.batch * L * kDimLatent;
-      const __nv_bfloat16* const kr_b = p.k_rope + (size_t)cur.w.batch * L * kDimRope;
+      const int gb = checked_index(cur.w.batch, p.batch, p.status);
+      const __nv_bfloat16* const kv_b = p.kv + (size_t)gb * L * kDimLatent;
+      const __nv_bfloat16* const kr_b = p.k_rope + (size_t)gb * L * kDimRope;
 #pragma unroll 2
       for (int i = 0; i < 8; ++i) {
         const int k = kq + 4 * i;  // key within this warp's half
         const int rk = __shfl_sync(0xffffffffu, row, k);
         const int krow = 32 * hf + k;
-        const uint32_t dst = stage + (uint32_t)krow * 128u + (uint32_t)((j8 ^ (krow & 7)) * 16);
+        const uint32_t dst = checked_smem(stage + (uint32_t)krow * 128u + (uint32_t)((j8 ^ (krow & 7)) * 16),
+                                          8u * kKyBlk + 16u, stage, kKyStage, p.status);
         const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
 #pragma unroll
         for (int b = 0; b < 8; ++b) cp_async_16(dst + (uint32_t)b * kKyBlk, src + b * 64);

@@ -279,15 +279,16 @@ __device__ __forceinline__ void mma_commit_mc(uint32_t bar, uint16_t cta_mask) {
 // 16-byte cp.async of 32 indexed rows into a swizzled K-major stage:
 // `nblk` 64-dim blocks of the latent row (+ the rope block when `rope`).
 __device__ __forceinline__ void gather_rows(uint32_t stage, const __nv_bfloat16* kv_b, const __nv_bfloat16* kr_b,
-                                            int row, int lane, bool rope) {
+                                            int row, int lane, bool rope, int32_t* status) {
   const int j8 = lane & 7;
   const int kq = lane >> 3;
 #pragma unroll 2
   for (int i = 0; i < kPrBN / 4; ++i) {
     const int k = kq + 4 * i;
     const int rk = __shfl_sync(0xffffffffu, row, k);
-    const uint32_t dst =
-        stage + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u + (uint32_t)((j8 ^ (k & 7)) * 16);
+    const uint32_t dst = checked_smem(
+        stage + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u + (uint32_t)((j8 ^ (k & 7)) * 16),
+        (rope ? 8u : 7u) * kBlk + 16u, stage, rope ? kKStage : kVStage, status);
     const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
 #pragma unroll
     for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * kBlk, src + kb * 64);
@@ -479,9 +480,10 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
             st_shared_v2(base + kOffMaskRing + 8u * (gt % kMaskRing), vbits, gt);
           }
         }
-        const int row = pcursor_row(p, idx_cur, L);  // clamped address; masked by the softmax
-        gather_rows(stage, p.kv + (size_t)cur.w.batch * L * kDimLatent,
-                    p.k_rope + (size_t)cur.w.batch * L * kDimRope, row, lane, true);
+        const int row = checked_index(pcursor_row(p, idx_cur, L), L, p.status);  // clamped; masked by the softmax
+        const int gb = checked_index(cur.w.batch, p.batch, p.status);
+        gather_rows(stage, p.kv + (size_t)gb * L * kDimLatent, p.k_rope + (size_t)gb * L * kDimRope, row, lane, true,
+                    p.status);
         cp_async_commit();
         const int idx_nx2 = pcursor_index(p, nx2, n_items, lane);  // consumed one round later
         cp_async_wait<0>();
@@ -657,7 +659,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
           float x[32];
           {
             uint32_t sv[32];
-            tmem_ld32(tmem + t_lane + kTmemS + i * kPrBN, sv);
+            tmem_ld32(checked_tmem(tmem + t_lane + kTmemS + i * kPrBN, tmem, 32u, kTmemCols, p.status), sv);
             tmem_wait_ld();
 #pragma unroll
             for (int k = 0; k < 32; ++k) x[k] = u2f(sv[k]);
@@ -791,8 +793,9 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       uint32_t n = 0;
       while (cur.item < n_items) {
         if (n > 0 && !(ok = wait_warp(bar(kVFree0 + s), (n - 1) & 1u, abort_flag))) break;
-        const int row = pcursor_row(p, idx_cur, L);  // invalid rows get P = 0
-        gather_rows(stage, p.kv + (size_t)cur.w.batch * L * kDimLatent, nullptr, row, lane, false);
+        const int row = checked_index(pcursor_row(p, idx_cur, L), L, p.status);  // invalid rows get P = 0
+        const int gb = checked_index(cur.w.batch, p.batch, p.status);
+        gather_rows(stage, p.kv + (size_t)gb * L * kDimLatent, nullptr, row, lane, false, p.status);
         cp_async_commit();
         const int idx_nx2 = pcursor_index(p, nx2, n_items, lane);
         cp_async_wait<0>();
@@ -863,6 +866,7 @@ __global__ void __launch_bounds__(kPrThreads, 1) fwd_pair_kernel(const FwdParams
       const int quad = warp & 3;
       const int part = (warp - kEpiWarp0) >> 2;
       const int cb0 = 32 * epi_chunk0(part), cb1 = 32 * epi_chunk0(part + 1);
+      if (kBoundsCheck && !(0 <= cb0 && cb0 < cb1 && cb1 <= (int)kTmemCols)) report_error(p.status, kErrBounds);
       const int row = quad * 32 + lane;
       const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
       const volatile uint32_t* const req = reinterpret_cast<const volatile uint32_t*>(sbase + kOffReq);

@@ -163,14 +163,16 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
         if (!ok) break;
       }
       sm.ids[s][lane] = idx_cur;  // validity is judged from the original index
-      const int row = min(max(idx_cur, 0), L - 1);
-      const __nv_bfloat16* kv_b = p.kv + (size_t)cur.w.batch * L * kDimLatent;
-      const __nv_bfloat16* kr_b = p.k_rope + (size_t)cur.w.batch * L * kDimRope;
+      const int row = checked_index(min(max(idx_cur, 0), L - 1), L, p.status);
+      const int gb = checked_index(cur.w.batch, p.batch, p.status);
+      const __nv_bfloat16* kv_b = p.kv + (size_t)gb * L * kDimLatent;
+      const __nv_bfloat16* kr_b = p.k_rope + (size_t)gb * L * kDimRope;
 #pragma unroll 2
       for (int i = 0; i < kStBN / 4; ++i) {
         const int key = kq + 4 * i;
         const int rk = __shfl_sync(0xffffffffu, row, key);
-        const uint32_t dst = stage + (uint32_t)(key * kStRow + j8 * 8) * 2u;
+        const uint32_t dst = checked_smem(stage + (uint32_t)(key * kStRow + j8 * 8) * 2u, 8u * 128u + 16u, stage,
+                                          (uint32_t)(kStBN * kStRow * 2), p.status);
         const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
 #pragma unroll
         for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * 128u, src + kb * 64);

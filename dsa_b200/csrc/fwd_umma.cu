@@ -191,6 +191,10 @@ __device__ __forceinline__ void store_o_part(const FwdParams& p, const Item& w, 
                                              int cb1, float l, float f) {
   uint32_t oa[32], ob[32];
   const int col0 = w.half * 256;
+  if (kBoundsCheck && (cb0 < 0 || cb1 > 256 || ((o_lane & 0xFFFFu) + (uint32_t)cb1 > kTmemCols))) {
+    report_error(p.status, kErrBounds);
+    return;
+  }
   if (p.split == 1) {
     // correctly rounded reciprocal (within an FP32 ulp of O / l); a row
     // without a valid index (l == 0) is written as 0
@@ -415,21 +419,23 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
       }
-      const int row = min(max(idx_cur, 0), L - 1);  // clamped address; masked below
+      const int row = checked_index(min(max(idx_cur, 0), L - 1), L, p.status);  // clamped address; masked below
       const uint32_t bits = __ballot_sync(0xffffffffu, (idx_cur >= 0) & (idx_cur < L));
       if (lane == 0) {
         *mask_s = bits;
         // the stage's previous tile (g - 4) is consumed, so its Full phase completed
         reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = s + kUmStages * n;
       }
-      const __nv_bfloat16* const kv_b = p.kv + (size_t)cur.w.batch * L * kDimLatent;
-      const __nv_bfloat16* const kr_b = p.k_rope + (size_t)cur.w.batch * L * kDimRope;
+      const int gb = checked_index(cur.w.batch, p.batch, p.status);
+      const __nv_bfloat16* const kv_b = p.kv + (size_t)gb * L * kDimLatent;
+      const __nv_bfloat16* const kr_b = p.k_rope + (size_t)gb * L * kDimRope;
 #pragma unroll 2
       for (int i = 0; i < kUmBN / 4; ++i) {
         const int k = kq + 4 * i;
         const int rk = __shfl_sync(0xffffffffu, row, k);
-        const uint32_t dst = stage + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u +
-                             (uint32_t)((j8 ^ (k & 7)) * 16);
+        const uint32_t dst = checked_smem(stage + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u +
+                                              (uint32_t)((j8 ^ (k & 7)) * 16),
+                                          8u * kKBlock + 16u, stage, kKStage, p.status);
         const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
 #pragma unroll
         for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * kKBlock, src + kb * 64);
@@ -613,7 +619,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         float x[32];
         {
           uint32_t sv[32];
-          tmem_ld32(tmem + t_lane + kTmemS + i * kUmBN, sv);
+          tmem_ld32(checked_tmem(tmem + t_lane + kTmemS + i * kUmBN, tmem, 32u, kTmemCols, p.status), sv);
           tmem_wait_ld();
 #pragma unroll
           for (int k = 0; k < 32; ++k) x[k] = u2f(sv[k]);

@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kWmThreads, 2) fwd_warp_mma_kernel(FwdParams p
   bid /= hgroups;
   const int sp = (int)(bid % p.split);
   const int token = (int)(bid / p.split);
-  const int batch = token / p.queries;
+  const int batch = checked_index(token / p.queries, p.batch, p.status);
   const int h0 = hg * kWmHeads;
 
   int kbeg, kend;
@@ -96,11 +96,13 @@ __global__ void __launch_bounds__(kWmThreads, 2) fwd_warp_mma_kernel(FwdParams p
       const int key = c / kChunksPerRow, part = c % kChunksPerRow;
       const int j = k0 + key;
       const int idx = (j < kend) ? __ldg(ids_t + j) : 0;
-      const int safe = min(max(idx, 0), L - 1);
+      const int safe = checked_index(min(max(idx, 0), L - 1), L, p.status);
       const __nv_bfloat16* src = part < kLatentChunks
                                      ? kv_b + (size_t)safe * kDimLatent + part * 8
                                      : kr_b + (size_t)safe * kDimRope + (part - kLatentChunks) * 8;
-      cp_async_16(smem_u32(&sm.k[stage][key * kWmRow + part * 8]), src);
+      cp_async_16(checked_smem(smem_u32(&sm.k[stage][key * kWmRow + part * 8]), 16u, smem_u32(sm.k[stage]),
+                               (uint32_t)(BN * kWmRow * 2), p.status),
+                  src);
     }
     if (tid < BN) {
       const int j = k0 + tid;
