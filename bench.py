@@ -56,11 +56,11 @@ DEFAULT_CONFIG = "prefill_h128"
 # rows that stay L2-resident after their first read). The bench reports
 # None for any other variant, shape or launch entry.
 TRAFFIC_MODEL = {
-    # fwd_pair_kernel, 512-query capture of prefill_h128 (one batch row):
-    # 351.3 MB read + 58.0 MB written. kv is re-read from DRAM in proportion
-    # to the queries (75.5 MB of kv per batch row does not stay in the L2
-    # next to the streamed q and outputs), so it all scales per query.
-    "prefill_h128": (0.0, (351.3e6 + 58.0e6) / 512),
+    # fwd_pair_kernel, full prefill_h128 launch (1-pass capture of ten
+    # launches): 10.49 GB read + 2.175 GB written. kv is re-read from DRAM in
+    # proportion to the queries (75.5 MB of kv per batch row does not stay in
+    # the L2 next to the streamed q and outputs), so it all scales per query.
+    "prefill_h128": (0.0, (10.49e9 + 2.175e9) / 16384),
     # union launch's fwd_pair_kernel, 1024-query capture of prefill_tp8:
     # 32.2 MB read + 0.17 MB written, of which the 9.4 MB kv + k_rope is
     # read once (it stays L2-resident) and the rest scales with the queries.
@@ -69,9 +69,12 @@ TRAFFIC_MODEL = {
     # same gathered rows per launch as decode_tp8; only L differs):
     # 152.8 MB read + 3.8 MB written.
     "decode_tp8": (0.0, (152.8e6 + 3.8e6) / 64),
-    # fwd_umma_kernel, capture of the full decode_b8 launch: 39.07 + 0.45 MB.
-    "decode_b8": (0.0, (39.07e6 + 0.45e6) / 16),
-    # fwd_umma_kernel, capture of the full decode_b1 launch: 2,586,368 B read.
+    # fwd_umma_kernel (cluster merge), capture of 18 full decode_b8 launches:
+    # 39.07 MB read + 0.07 MB written (the FP32 partials stay in the L2).
+    "decode_b8": (0.0, (39.07e6 + 0.07e6) / 16),
+    # fwd_umma_kernel, capture of a full decode_b1 launch with split 32 and
+    # a separate merge (before the cluster merge; the DRAM reads are the
+    # gathered rows and Q either way): 2,586,368 B read.
     "decode_b1": (0.0, 2586368.0),
 }
 
@@ -218,7 +221,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -297,9 +300,26 @@ class CpuSample:
             self.oracle.reference_forward(*compact)
         return (time.perf_counter() - t0) * self.total / self.rows
 
+    def warm(self, seconds=2.0):
+        """Untimed passes until the host threads reach their steady state."""
+        end = time.perf_counter() + seconds
+        self.run()
+        while time.perf_counter() < end:
+            self.run()
+
+    def measure(self, seconds):
+        """Median of full-call times over passes that fill at least `seconds`
+        (at least one pass); returns (median seconds per call, passes)."""
+        per_call, spent = [], 0.0
+        while spent < seconds or not per_call:
+            t0 = time.perf_counter()
+            per_call.append(self.run())
+            spent += time.perf_counter() - t0
+        return statistics.median(per_call), len(per_call)
+
     def describe(self, passes):
         return (f"first {self.rows} of {self.total} queries ({100.0 * self.rows / self.total:.2f} %) per pass, "
-                f"median of {passes} timed pass(es) after one untimed pass; FP32 torch oracle of "
+                f"median of {passes} timed pass(es) after ~2 s of untimed passes; FP32 torch oracle of "
                 f"tools/review.py:123-145 (HF32/TF32 off), scaled to a full call")
 
 
@@ -330,11 +350,14 @@ def run_reference(args, shape):
     b, s, h, length, k = shape
     sample = CpuSample(data, shape)
     data = None
-    per_call = []
+    sample.warm()
+    # each step: the median over passes that fill >= 0.3 s (one pass when longer)
+    per_call, passes = [], 0
     for i in range(args.warmup + args.steps):
-        t = sample.run()
+        t, n = sample.measure(0.3)
         if i >= args.warmup:
             per_call.append(t)
+            passes += n
     us = statistics.median(per_call) * 1e6
     threads = sample.threads
     line = {
@@ -344,7 +367,8 @@ def run_reference(args, shape):
         "config": {"workload": args.config, "B": b, "SQ": s, "H": h, "L": length, "TOPK": k,
                    "index_variant": args.variant, "seed": SEED},
         "cpu_baseline": {"value": us, "unit": "us/call", "cores": threads, "kind": "port",
-                         "sample": sample.describe(args.steps) + "; one pass per step"},
+                         "sample": sample.describe(passes) + "; per step the median over >= 0.3 s of passes, "
+                                   "the line's value the median over steps"},
         "e2e": {"value": us, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -365,7 +389,6 @@ def main():
                          "(selects a kernel family, e.g. 128,32,1,256 for the split-V family)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--e2e-steps", type=int, default=None)
-    ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -425,13 +448,16 @@ def main():
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches_total = 0
-    # a short timed region (decode) is shorter than the 50 ms between clock
-    # samples: the same steps then also run untimed for ~0.3 s just before
-    # it, inside the sampled window, so the clock record covers this load
+    # a timed region of a few milliseconds (decode) fits between two 20 ms
+    # clock samples: the same steps then also run untimed for ~60 ms just
+    # before it, inside the sampled window, so the clock record covers this
+    # load. Longer regions (prefill) are sampled as they are: extra load
+    # before them would only push the GPU into its power cap earlier.
     t0 = time.perf_counter()
     step()
     torch.cuda.synchronize()
-    load_steps = 0 if (time.perf_counter() - t0) * args.steps >= 0.25 else max(1, int(0.3 / max(time.perf_counter() - t0, 1e-5)))
+    step_s = max(time.perf_counter() - t0, 1e-5)
+    load_steps = 0 if step_s * args.steps >= 0.02 else int(0.06 / step_s)
     with ClockSampler(local) as clocks:
         time.sleep(0.3)  # let nvidia-smi start sampling before the timed region
         t_host0 = time.time()
@@ -590,19 +616,27 @@ def main():
                          "queries": [sharded.shard_bounds(b * s, world, r)[1] - sharded.shard_bounds(b * s, world, r)[0]
                                      for r in range(world)]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        dev_data = [t.to(device, non_blocking=True) for t in host_in[0]]  # one GPU: one piece, all queries
-        torch.cuda.synchronize()
-        sample = CpuSample(dev_data, shape)
-        dev_data = None
-        sample.run()  # untimed pass
-        per_call, spent = [], 0.0
-        while spent < args.cpu_budget or not per_call:
-            t0 = time.perf_counter()
-            per_call.append(sample.run())
-            spent += time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": statistics.median(per_call) * 1e6, "unit": "us/call",
-                                "cores": sample.threads, "kind": "port",
-                                "sample": sample.describe(len(per_call)) + f" (~{args.cpu_budget:.0f} s)"}
+        # the reference arm itself (bench.py --impl reference, same sample and
+        # method), in a fresh child process after this process's GPU timing
+        cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference", "--config",
+               args.config if not args.shape else DEFAULT_CONFIG, "--variant", args.variant, "--steps", "5",
+               "--warmup", "3"] + (["--shape", args.shape] if args.shape else [])
+        env = dict(os.environ, WORLD_SIZE="1", RANK="0", LOCAL_RANK="0")
+        res = subprocess.run(cmd, capture_output=True, text=True, env=env)
+        ref = None
+        for ln in reversed(res.stdout.strip().splitlines()):
+            try:
+                ref = json.loads(ln)
+                break
+            except json.JSONDecodeError:
+                continue
+        if res.returncode == 0 and ref is not None and "cpu_baseline" in ref:
+            cb = dict(ref["cpu_baseline"])
+            cb["sample"] += "; measured by bench.py --impl reference (5 steps, 3 warm-up) in a child process of this run"
+            line["cpu_baseline"] = cb
+        else:
+            line["cpu_baseline"] = {"value": None, "unit": "us/call", "cores": None, "kind": "port",
+                                    "sample": f"reference arm failed (rc {res.returncode}): {res.stderr[-200:]}"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
