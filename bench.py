@@ -390,6 +390,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--direct", action="store_true",
+                    help="time direct launches of the prepared forward instead of CUDA-graph replay")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -432,7 +434,11 @@ def main():
             pl.run()
 
     def step():
-        graph.replay()
+        if args.direct:
+            for pl in plans:
+                pl.run()
+        else:
+            graph.replay()
         return plans[-1].outputs, kernels_per_step
 
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
@@ -591,7 +597,8 @@ def main():
                    "index_variant": args.variant, "seed": SEED,
                    "parallelism": f"query-shard x{world}, kv replicated",
                    "l2": "flushed between timed iterations (256 MiB write outside the events)",
-                   "timed": "CUDA-graph replay of ForwardPlan.run (one graph per step)",
+                   "timed": ("direct launches of ForwardPlan.run" if args.direct
+                             else "CUDA-graph replay of ForwardPlan.run (one graph per step)"),
                    "launch": {"family": int(plans[0].launch.family), "split": int(plans[0].launch.split)}},
         "calls_per_s": 1e6 / us,
         "tflops": flops / (us * 1e-6) / 1e12,

@@ -46,9 +46,9 @@ struct Layout {
 };
 
 // Split partials (dsa/api.py:111-113): numerator [T, S, H, 512] FP32 and
-// max / sum [T, S, H] FP32. The umma family's cluster merge keeps the same
-// numerator and, instead of max / sum, (max, sum) pairs per value half
-// [T, 2, S, H] (each cluster merges one half on its own).
+// max / sum [T, S, H] FP32. The umma family's cluster merge keeps the
+// numerator as [T, 2, S, H, 256] and, instead of max / sum, (max, sum)
+// pairs per value half [T, 2, S, H] (each cluster merges one half on its own).
 Layout partial_layout(int64_t tokens, int64_t heads, int64_t split, bool cluster_merge = false) {
   Layout lay{0, 0, 0, 0};
   if (split <= 1) return lay;

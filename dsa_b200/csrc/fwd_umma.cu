@@ -80,6 +80,7 @@ enum Bar {
   kEmpty0 = kFull0 + kUmStages,
   kQFull = kEmpty0 + kUmStages,  // this item's Q is loaded (softmax warps)
   kQSeen,                        // every QK issuer has seen this item's Q (issuers)
+  kQHelp,                        // the issuer warps' part of the first item's Q is loaded
   kSFull0,
   kSFree0 = kSFull0 + kQkIssuers,
   kPFull0 = kSFree0 + kQkIssuers,  // P buffer b written (tiles g with g % 2 == b)
@@ -102,6 +103,17 @@ constexpr uint32_t kTmemQ = kTmemS + kQkIssuers * kUmBN;    // 352
 
 static_assert(kOffK % 1024 == 0 && kKStage % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms");
 static_assert(kTmemQ + kQTmemDims / 2 == kTmemCols, "TMEM budget");
+static_assert((uint32_t)kUmHeads * 1024u <= kUmStages * kKStage, "the merged epilogue stages O in the stage buffers");
+// Largest slice the merged epilogue loads: ceil(128 / S) rows of 1 KB from each of S splits.
+constexpr uint32_t max_slice_bytes(int s = 2) {
+  return s > kUmMaxClusterSplit ? 0u
+                                : ((uint32_t)((kUmHeads + s - 1) / s * s) * 1024u > max_slice_bytes(s + 1)
+                                       ? (uint32_t)((kUmHeads + s - 1) / s * s) * 1024u
+                                       : max_slice_bytes(s + 1));
+}
+static_assert(max_slice_bytes() <= kUmStages * kKStage, "the merged epilogue loads its slice into the stage buffers");
+static_assert((uint32_t)(kUmHeads / 2 + 1) * 16u * 4u <= 2u * kPBytes, "the slice weights fit the P buffers");
+static_assert((uint32_t)kUmHeads * 8u <= kOffBar - kOffEpi, "the pushed row statistics fit the epilogue slots");
 static_assert(kQTmemDims % 64 == 0, "Q TMEM part is a whole number of 64-dim blocks");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kOffStageTile + 4u * kUmStages <= kOffEpi, "stage tile words");
@@ -231,22 +243,82 @@ __device__ __forceinline__ void store_o_part(const FwdParams& p, const Item& w, 
   }
 }
 
+// Step 3 of the merged epilogue for S splits: rows [r0, r0 + nrows) x 256
+// columns, one 16-byte chunk (row, 4 columns) per unit; each thread loads
+// the S partial chunks of up to 24 / S units at once (plain L2 loads: every
+// load of a batch is in flight together), then sums them in split order with
+// the rows' weights and writes BF16. The chunks of split `own_split` (the
+// CTA's own rows, when it kept them) are read from its staging buffer.
+template <int S>
+__device__ __forceinline__ void slice_sum(const FwdParams& p, const float4* part, const float4* own,
+                                          const float* wts, int r0, int nrows, int own_split, int token, int half) {
+  constexpr int kUB = 24 / S > 0 ? 24 / S : 1;  // units per thread per batch
+  const int nunits = nrows * 64;
+#pragma unroll 1
+  for (int u0 = threadIdx.x; u0 < nunits; u0 += kUmThreads * kUB) {
+    float4 v[kUB][S];
+#pragma unroll
+    for (int b = 0; b < kUB; ++b) {
+      const int u = u0 + b * kUmThreads;
+      if (u < nunits) {
+        const int rr = r0 + (u >> 6);
+        const int pos = (u & 63) ^ (rr & 7);
+#pragma unroll
+        for (int k = 0; k < S; ++k)
+          v[b][k] = k == own_split ? own[rr * 64 + pos] : __ldcg(part + ((size_t)k * kUmHeads + rr) * 64 + pos);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kUB; ++b) {
+      const int u = u0 + b * kUmThreads;
+      if (u < nunits) {
+        const int lr = u >> 6, ch = u & 63;
+        const float* const w = wts + lr * 16;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+          const float wk = w[k];
+          acc.x = fmaf(wk, v[b][k].x, acc.x);
+          acc.y = fmaf(wk, v[b][k].y, acc.y);
+          acc.z = fmaf(wk, v[b][k].z, acc.z);
+          acc.w = fmaf(wk, v[b][k].w, acc.w);
+        }
+        uint2 h;
+        h.x = pack_bf16x2(acc.x, acc.y);
+        h.y = pack_bf16x2(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(p.out + ((size_t)token * kUmHeads + r0 + lr) * kDimLatent + half * 256 + ch * 4) =
+            h;
+      }
+    }
+  }
+}
+
 // Epilogue of the cluster-merge launch, run by all 384 threads of every CTA
-// of the cluster (the two cluster barriers are always taken, also by a CTA
-// that gave up on a wait; it then skips the work). The CTA of split sp holds
-// O_sp (128 rows x 256 columns of its value half, relative to its running
-// max m_used) in TMEM and, per row, (m_sp, l, f) in shared memory, with
-// l relative to m_used and f = exp(m_used - m_sp). The merge of
+// of the cluster (the cluster barrier is always taken, also by a CTA that
+// gave up on a wait; it then skips the work). The CTA of split sp holds O_sp
+// (128 rows x 256 columns of its value half, relative to its running max
+// m_used) in TMEM and, per row, (m_sp, l, f) in shared memory, with l
+// relative to m_used and f = exp(m_used - m_sp). The merge of
 // dsa/merge.py:13-91 then is: M = max_s m_s, w_s = exp(m_s - M),
-// L = sum_s w_s l_s, O = sum_s (w_s f_s / L) O_s.
-//   1. each CTA writes its rows' (m_sp, l f) to the L2;  cluster barrier;
-//   2. each CTA reads every split's statistics of its rows, scales its O by
-//      w_sp f / L and writes it (FP32) to the L2; the owner of a row (half 0)
-//      writes softmax_max / softmax_sum;  cluster barrier;
-//   3. CTA rank r sums rows [128 r / S, 128 (r + 1) / S) over the S splits
-//      and writes them as BF16.
-// Statistics: [token][half][split][128] (m, l); partials: [token][split][128][512].
-__device__ __forceinline__ void merged_epilogue(const FwdParams& p, uint8_t* sbase, uint32_t tmem, bool live) {
+// L = sum_s w_s l_s f_s, O = sum_s (w_s / L) (f_s O_s).
+//   1. each CTA publishes its rows' (m_sp, l f) and f O_sp, without waiting
+//      for the other splits: O is staged in the free stage buffers (rows of
+//      1 KB, 16-byte chunks XOR-swizzled by row % 8 so a warp's stores hit
+//      distinct banks) and written to the L2 by bulk copies; the statistics
+//      go to the L2 too, or, when S divides 128 (every owner has 128 / S
+//      rows), straight into the owner's shared memory (DSMEM stores), and
+//      the rows this CTA owns stay where they are staged;
+//   2. cluster barrier;
+//   3. CTA rank r computes the weights w_s / L of its rows [128 r / S,
+//      128 (r + 1) / S) from the statistics (the owner of a row in half 0
+//      writes softmax_max / softmax_sum), loads the rows of every split
+//      from the L2, sums them in split order and writes them as BF16.
+// Partials: [token][half][split][128][256] FP32, chunk-swizzled as staged;
+// statistics: [token][half][split][128] (m, l f), or [split][row - r0] in
+// the owner's shared memory (the epilogue slots, unused by this launch).
+__device__ __forceinline__ void merged_epilogue(const FwdParams& p, uint8_t* sbase, uint32_t base, uint32_t tmem,
+                                                volatile int* abort_flag) {
+  const bool live = *abort_flag == 0;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = p.split;
@@ -254,23 +326,91 @@ __device__ __forceinline__ void merged_epilogue(const FwdParams& p, uint8_t* sba
   const int cl = (int)blockIdx.x / S;
   const int token = cl >> 1, half = cl & 1;
   const float c = p.scale_log2;
-  float2* const pstat = reinterpret_cast<float2*>(p.part_max);
-  const float4* const srow = reinterpret_cast<const float4*>(sbase + kOffQ);
-  const int row = (warp & 3) * 32 + lane;  // the head row of warps 4..11
   const int r0 = sp * kUmHeads / S, r1 = (sp + 1) * kUmHeads / S;
-  if (live && warp >= kSoftWarp0) {
-    const float4 st = srow[row];
-    pstat[((size_t)cl * S + sp) * kUmHeads + row] = make_float2(st.x, st.y * st.z);
-  }
-  cluster_sync();
+  const int nrows = r1 - r0;
+  const bool even = (kUmHeads % S) == 0;  // S in {2, 4, 8, 16}: 128 / S rows per owner
+  float2* const sstat = reinterpret_cast<float2*>(sbase + kOffEpi);
+  float4* const part = reinterpret_cast<float4*>(p.part_num) + (size_t)cl * S * kUmHeads * 64;  // this (token, half)
+  float2* const pstat = reinterpret_cast<float2*>(p.part_max) + (size_t)cl * S * kUmHeads;
   if (live && warp >= kQkWarp0) {
     tc_fence_after();
-    const float4 st = srow[row];
-    const float2* const rs = pstat + (size_t)cl * S * kUmHeads + row;
+    const int row = (warp & 3) * 32 + lane;
+    const float4 st = reinterpret_cast<const float4*>(sbase + kOffQ)[row];
+    const bool lower = warp >= kSoftWarp0;  // columns 0..127 of the half, else 128..255
+    if (lower) {
+      const float2 v = make_float2(st.x, st.y * st.z);
+      if (even) {
+        cluster_wait();  // every CTA of the cluster runs (first barrier phase)
+        const int owner = row / nrows;
+        st_shared_cluster_f2(mapa_shared(base + kOffEpi + (uint32_t)(sp * nrows + row - owner * nrows) * 8u,
+                                         (uint32_t)owner),
+                             v);
+      } else {
+        pstat[(size_t)sp * kUmHeads + row] = v;
+      }
+    }
+    const float f = st.z;
+    const uint32_t o_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + kTmemO + (lower ? 0u : 128u);
+    float4* const srow = reinterpret_cast<float4*>(sbase + kOffK + (uint32_t)row * 1024u);
+    const int ch0 = lower ? 0 : 32;  // first 16-byte chunk of this thread's columns
+#pragma unroll 1
+    for (int cb = 0; cb < 128; cb += 64) {
+      uint32_t o[64];
+      tmem_ld32(o_lane + cb, o);
+      tmem_ld32(o_lane + cb + 32, o + 32);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int ch = ch0 + cb / 4 + j;
+        srow[checked_index(ch ^ (row & 7), 64, p.status)] =
+            make_float4(__uint_as_float(o[4 * j]) * f, __uint_as_float(o[4 * j + 1]) * f,
+                        __uint_as_float(o[4 * j + 2]) * f, __uint_as_float(o[4 * j + 3]) * f);
+      }
+    }
+  }
+  // the threads that did not take the first barrier phase above wait for it
+  // here, so every thread of the CTA waits on it exactly once
+  if (!(live && even && warp >= kSoftWarp0)) cluster_wait();
+  tc_fence_before();
+  fence_proxy_async_smem();  // the staged rows -> visible to the bulk copies
+  __syncthreads();
+  // bulk copies are issued by lane 0 of different warps (copies issued by the
+  // lanes of one warp go out one after another)
+  if (live && warp >= kQkWarp0 && lane == 0) {
+    const int w = warp - kQkWarp0;  // 0..7
+    float4* const dst = part + (size_t)sp * kUmHeads * 64;
+    const uint32_t src = base + kOffK;
+    bool issued = false;
+    if (even) {  // rows [0, r0) and [r1, 128): the owned rows stay staged
+      if (w == 0 && r0 > 0) {
+        bulk_store_global(dst, src, (uint32_t)r0 * 1024u);
+        issued = true;
+      }
+      if (w == 1 && r1 < kUmHeads) {
+        bulk_store_global(dst + (size_t)r1 * 64, src + (uint32_t)r1 * 1024u, (uint32_t)(kUmHeads - r1) * 1024u);
+        issued = true;
+      }
+    } else {  // 16 head rows (16 KB) per copy
+      bulk_store_global(dst + (size_t)w * 16 * 64, src + (uint32_t)w * 16384u, 16384u);
+      issued = true;
+    }
+    if (issued) {
+      bulk_commit_group();
+      bulk_wait_group_all();
+      fence_proxy_async_global();
+    }
+  }
+  cluster_sync();  // every split's statistics and partial rows are published
+  if (!live) return;
+  // weights w_s / L of the owned rows -> the (free) P buffers [row - r0][16]
+  float* const wts = reinterpret_cast<float*>(sbase + kOffP);
+  if (threadIdx.x < (unsigned)nrows) {
+    const int lr = (int)threadIdx.x;
+    const int row = r0 + lr;
     float2 ms[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-      if (k < S) ms[k] = __ldcg(rs + (size_t)k * kUmHeads);
+      if (k < S) ms[k] = even ? sstat[k * nrows + lr] : __ldcg(pstat + (size_t)k * kUmHeads + row);
     float M = kNegFltMax;
 #pragma unroll
     for (int k = 0; k < 16; ++k)
@@ -281,50 +421,29 @@ __device__ __forceinline__ void merged_epilogue(const FwdParams& p, uint8_t* sba
       if (k < S && ms[k].y > 0.f) L += ms[k].y * ex2((ms[k].x - M) * c);
     // an all-masked split (l = 0, O = 0) and a row without any valid index
     // (L = 0: output 0) contribute nothing
-    const float factor = L > 0.f ? st.z * ex2((st.x - M) * c) / L : 0.f;
-    const bool lower = warp >= kSoftWarp0;  // columns 0..127 of the half, else 128..255
-    float* dst = p.part_num + (((size_t)token * S + sp) * kUmHeads + row) * kDimLatent + half * 256 + (lower ? 0 : 128);
-    const bool wide = (reinterpret_cast<uintptr_t>(p.part_num) & 31u) == 0;
-    const uint32_t o_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + kTmemO + (lower ? 0u : 128u);
-    uint32_t o[32];
-#pragma unroll 1
-    for (int cb = 0; cb < 128; cb += 32) {
-      tmem_ld32(o_lane + cb, o);
-      tmem_wait_ld();
-      store_f32_row32(dst + cb, o, factor, wide);
-    }
-    if (lower && half == 0 && row >= r0 && row < r1) {
+    const float rl = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < S) wts[lr * 16 + k] = ms[k].y > 0.f ? ex2((ms[k].x - M) * c) * rl : 0.f;
+    if (half == 0) {
       const size_t orow = (size_t)token * kUmHeads + row;
       p.out_max[orow] = final_max(M, L, p.scale_div);
       p.out_sum[orow] = L;
     }
   }
-  tc_fence_before();
-  cluster_sync();
-  if (live) {
-    // rows [r0, r1) x 256 columns of this half: 64 groups of four columns per row
-    const int groups = (r1 - r0) * 64;
-    const size_t sstride = (size_t)kUmHeads * kDimLatent / 4;  // float4s between splits
-    const float4* const src = reinterpret_cast<const float4*>(p.part_num) +
-                              (((size_t)token * S) * kUmHeads) * (kDimLatent / 4) + half * 64;
-#pragma unroll 1
-    for (int i = threadIdx.x; i < groups; i += kUmThreads) {
-      const int rr = r0 + i / 64, g4 = i % 64;
-      const float4* sp4 = src + (size_t)rr * (kDimLatent / 4) + g4;
-      float4 acc = __ldcg(sp4);
-#pragma unroll 4
-      for (int k = 1; k < S; ++k) {
-        const float4 v = __ldcg(sp4 + k * sstride);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-      uint2 h;
-      h.x = pack_bf16x2(acc.x, acc.y);
-      h.y = pack_bf16x2(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(p.out + ((size_t)token * kUmHeads + rr) * kDimLatent + half * 256 + g4 * 4) = h;
-    }
+  __syncthreads();  // the weights are in shared memory
+  const float4* const own = reinterpret_cast<const float4*>(sbase + kOffK);
+  switch (S) {
+#define DSA_SLICE_SUM(n) \
+  case n:                \
+    slice_sum<n>(p, part, own, wts, r0, nrows, even ? sp : -1, token, half); \
+    break;
+    DSA_SLICE_SUM(2) DSA_SLICE_SUM(3) DSA_SLICE_SUM(4) DSA_SLICE_SUM(5) DSA_SLICE_SUM(6) DSA_SLICE_SUM(7)
+    DSA_SLICE_SUM(8) DSA_SLICE_SUM(9) DSA_SLICE_SUM(10) DSA_SLICE_SUM(11) DSA_SLICE_SUM(12) DSA_SLICE_SUM(13)
+    DSA_SLICE_SUM(14) DSA_SLICE_SUM(15) DSA_SLICE_SUM(16)
+#undef DSA_SLICE_SUM
+    default:
+      break;
   }
 }
 
@@ -353,6 +472,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     }
     mbar_init(bar(kQFull), kSoftWarps);
     mbar_init(bar(kQSeen), kQkIssuers);
+    mbar_init(bar(kQHelp), 4);
     for (int s = 0; s < kUmStages; ++s) reinterpret_cast<volatile uint32_t*>(sbase + kOffStageTile)[s] = 0xffffffffu;
     for (int k = 0; k < kQkIssuers; ++k) {
       mbar_init(bar(kSFull0 + k), 1);
@@ -376,6 +496,10 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // cluster-merge launch: the first phase of the cluster barrier completes
+  // once every CTA of the cluster runs; the merged epilogue waits on it
+  // before it writes into a peer's shared memory
+  if constexpr (kCM) cluster_arrive_relaxed();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sbase + kOffTmemSlot);
 
   const int n_items = p.tokens * p.split * 2;
@@ -392,6 +516,42 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     tc_fence_before();
     __syncwarp();
     return true;
+  };
+
+  // The first item's Q is loaded by eight warps at once: the issuer warps
+  // 4..7 (idle until the first tile) take latent dims 192..319 (TMEM) and
+  // 448..511 plus the rope dims (shared memory) of the head rows of their
+  // TMEM lane quadrant; the softmax warps take the rest.
+  auto q_help = [&](int item) {
+    const int row = (warp & 3) * 32 + lane;
+    const size_t qrow = (size_t)make_item(p, item).token * kUmHeads + row;
+    const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
+    const uint32_t qdst = base + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
+#pragma unroll
+    for (int k = 16; k < 24; ++k)  // latent dims 448..511: the third shared-memory block
+      cp_async_16(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16), src + kQTmemDims / 8 + k);
+    const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cp_async_16(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16), rsrc + k);
+    cp_async_commit();
+    uint32_t r[64];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint4 v = __ldg(src + 24 + k);  // dims 192..319
+      r[4 * k] = v.x;
+      r[4 * k + 1] = v.y;
+      r[4 * k + 2] = v.z;
+      r[4 * k + 3] = v.w;
+    }
+    const uint32_t t_lane = (uint32_t)((warp & 3) * 32) << 16;
+    tmem_st32(tmem + t_lane + kTmemQ + 96, r);
+    tmem_st32(tmem + t_lane + kTmemQ + 128, r + 32);
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(kQHelp));
   };
 
   if (warp < kGatherWarps) {
@@ -463,11 +623,13 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const uint32_t d = tmem + kTmemS + i * kUmBN;
     uint32_t g = 0, it = 0, n = 0;  // n: tiles this issuer ran
     bool ok = true;
+    if (item0 < n_items) q_help(item0);
     for (int item = item0; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
       // Every issuer observes every item's Q (even without a tile in it) and
       // acknowledges, so no issuer can fall a barrier phase behind.
       ok = wait_warp(bar(kQFull), it & 1u, abort_flag, lim);
+      if (ok && it == 0) ok = wait_warp(bar(kQHelp), 0u, abort_flag, lim);
       if (!ok) break;
       if (elect_one()) mbar_arrive(bar(kQSeen));
       __syncwarp();
@@ -516,6 +678,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const uint32_t idesc_pv = idesc_bf16(128, 256, false, true);
     uint32_t g = 0, it = 0;
     bool ok = true;
+    if (item0 < n_items) q_help(item0);
     for (int item = item0; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
       const uint32_t vblk = (uint32_t)w.half * 4u * kKBlock;  // first latent block of this V half
@@ -568,38 +731,46 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       // issuer has seen the previous item's Q.
       if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag, lim))) break;
       {
+        // the first item: latent dims 0..191 (TMEM) and 320..447 (shared
+        // memory) here, the rest by the issuer warps; later items: all of it
+        const bool first = it == 0;
         const size_t qrow = (size_t)w.token * kUmHeads + row;
         const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
         // dims 320..511 and the rope dims -> shared memory, asynchronously
         const uint32_t qdst = base + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
 #pragma unroll
         for (int k = 0; k < (kDimLatent - kQTmemDims) / 8; ++k)  // latent dims 320..511: 3 blocks
-          cp_async_16(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16), src + kQTmemDims / 8 + k);
-        const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
+          if (k < 16 || !first)
+            cp_async_16(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16), src + kQTmemDims / 8 + k);
+        if (!first) {
+          const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) cp_async_16(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16), rsrc + k);
+          for (int k = 0; k < 8; ++k) cp_async_16(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16), rsrc + k);
+        }
         cp_async_commit();
-        // dims 0..319 -> TMEM, the next chunk's loads in flight while one is stored
-        uint4 qa[8], qb[8];
+        // dims 0..319 -> TMEM in 64-dim chunks, three chunks' loads in flight
+        const int nch = first ? 3 : kQTmemDims / 64;
+        uint4 qa[24];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) qa[k] = __ldg(src + k);
+        for (int k = 0; k < 24; ++k) qa[k] = __ldg(src + k);
 #pragma unroll
         for (int ch = 0; ch < kQTmemDims / 64; ++ch) {
-          if (ch + 1 < kQTmemDims / 64) {
+          if (ch < nch) {
+            uint32_t r[32];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) qb[k] = __ldg(src + (ch + 1) * 8 + k);
+            for (int k = 0; k < 8; ++k) {
+              const uint4 v = qa[(ch % 3) * 8 + k];
+              r[4 * k] = v.x;
+              r[4 * k + 1] = v.y;
+              r[4 * k + 2] = v.z;
+              r[4 * k + 3] = v.w;
+            }
+            tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
+            if (ch + 3 < nch) {
+#pragma unroll
+              for (int k = 0; k < 8; ++k) qa[(ch % 3) * 8 + k] = __ldg(src + (ch + 3) * 8 + k);
+            }
           }
-          uint32_t r[32];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            r[4 * k] = qa[k].x;
-            r[4 * k + 1] = qa[k].y;
-            r[4 * k + 2] = qa[k].z;
-            r[4 * k + 3] = qa[k].w;
-          }
-          tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) qa[k] = qb[k];
         }
         cp_async_wait<0>();
         fence_proxy_async_smem();
@@ -742,7 +913,9 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     tc_fence_before();
     __syncthreads();
   }
-  if constexpr (kCM) merged_epilogue(p, sbase, tmem, *abort_flag == 0);
+  if constexpr (kCM) {
+    merged_epilogue(p, sbase, base, tmem, abort_flag);
+  }
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

@@ -160,11 +160,29 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t remote_dst, uint32_t 
       "r"(local_src), "r"(bytes), "r"(remote_bar)
       : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory to global memory, tracked by bulk groups.
+__device__ __forceinline__ void bulk_store_global(void* gdst, uint32_t local_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
+               "r"(local_src), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until this thread's bulk copy groups have completed (writes performed).
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Wait until at most N of this thread's bulk copy groups still read their source.
 template <int N>
 __device__ __forceinline__ void bulk_wait_group_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Split cluster barrier: arrive (no ordering) now, wait (acquire) later.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// 8 bytes into a cluster peer's shared memory (shared::cluster address from mapa).
+__device__ __forceinline__ void st_shared_cluster_f2(uint32_t addr, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
@@ -174,6 +192,10 @@ __device__ __forceinline__ void cluster_sync() {
 // ---- fences -----------------------------------------------------------------------
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Async-proxy global writes (bulk copies) -> ordered before later generic operations.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
