@@ -264,8 +264,12 @@ __device__ __forceinline__ void slice_sum(const FwdParams& p, const float4* part
         const int rr = r0 + (u >> 6);
         const int pos = (u & 63) ^ (rr & 7);
 #pragma unroll
-        for (int k = 0; k < S; ++k)
-          v[b][k] = k == own_split ? own[rr * 64 + pos] : __ldcg(part + ((size_t)k * kUmHeads + rr) * 64 + pos);
+        for (int k = 0; k < S; ++k) {
+          if (k == own_split)
+            v[b][k] = own[rr * 64 + pos];
+          else
+            v[b][k] = __ldcg(part + ((size_t)k * kUmHeads + rr) * 64 + pos);
+        }
       }
     }
 #pragma unroll
@@ -408,23 +412,33 @@ __device__ __forceinline__ void merged_epilogue(const FwdParams& p, uint8_t* sba
     const int lr = (int)threadIdx.x;
     const int row = r0 + lr;
     float2 ms[16];
+    if (even) {  // pushed into this CTA's shared memory
 #pragma unroll
-    for (int k = 0; k < 16; ++k)
-      if (k < S) ms[k] = even ? sstat[k * nrows + lr] : __ldcg(pstat + (size_t)k * kUmHeads + row);
+      for (int k = 0; k < 16; ++k)
+        if (k < S) ms[k] = sstat[k * nrows + lr];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (k < S) ms[k] = __ldcg(pstat + (size_t)k * kUmHeads + row);
+    }
     float M = kNegFltMax;
 #pragma unroll
     for (int k = 0; k < 16; ++k)
       if (k < S) M = fmaxf(M, ms[k].x);
+    // an all-masked split (l = 0, O = 0) and a row without any valid index
+    // (L = 0: output 0) contribute nothing
+    float e[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) e[k] = (k < S && ms[k].y > 0.f) ? ex2((ms[k].x - M) * c) : 0.f;
     float L = 0.f;
 #pragma unroll
     for (int k = 0; k < 16; ++k)
-      if (k < S && ms[k].y > 0.f) L += ms[k].y * ex2((ms[k].x - M) * c);
-    // an all-masked split (l = 0, O = 0) and a row without any valid index
-    // (L = 0: output 0) contribute nothing
+      if (k < S) L = fmaf(ms[k].y, e[k], L);
     const float rl = L > 0.f ? 1.f / L : 0.f;
+    float4* const w4 = reinterpret_cast<float4*>(wts + lr * 16);
 #pragma unroll
-    for (int k = 0; k < 16; ++k)
-      if (k < S) wts[lr * 16 + k] = ms[k].y > 0.f ? ex2((ms[k].x - M) * c) * rl : 0.f;
+    for (int k = 0; k < 16; k += 4)
+      if (k < S) w4[k / 4] = make_float4(e[k] * rl, e[k + 1] * rl, e[k + 2] * rl, e[k + 3] * rl);
     if (half == 0) {
       const size_t orow = (size_t)token * kUmHeads + row;
       p.out_max[orow] = final_max(M, L, p.scale_div);
