@@ -55,6 +55,7 @@ constexpr int kPvWarp = kQkWarp0 + kQkIssuers;          // 7
 constexpr int kSoftWarp0 = kPvWarp + 1;                 // 8
 constexpr int kSoftWarps = 4;
 constexpr int kUmThreads = 32 * (kSoftWarp0 + kSoftWarps);  // 384
+constexpr int kThreadsQ = kUmThreads - 32;                   // warps 1..11 load the first item's Q
 constexpr int kUmHeads = 128;
 constexpr int kQTmemDims = 320;    // Q dims kept in TMEM (A operand of TS steps)
 constexpr int kQkSteps = kDimQK / 16;        // 36
@@ -532,39 +533,80 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     return true;
   };
 
-  // The first item's Q is loaded by eight warps at once: the issuer warps
-  // 4..7 (idle until the first tile) take latent dims 192..319 (TMEM) and
-  // 448..511 plus the rope dims (shared memory) of the head rows of their
-  // TMEM lane quadrant; the softmax warps take the rest.
-  auto q_help = [&](int item) {
-    const int row = (warp & 3) * 32 + lane;
-    const size_t qrow = (size_t)make_item(p, item).token * kUmHeads + row;
-    const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
-    const uint32_t qdst = base + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
-#pragma unroll
-    for (int k = 16; k < 24; ++k)  // latent dims 448..511: the third shared-memory block
-      cp_async_16(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16), src + kQTmemDims / 8 + k);
-    const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) cp_async_16(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16), rsrc + k);
+  // The first item's Q, loaded by warps 1..11 together with coalesced
+  // 16-byte loads (a warp reads 512 contiguous bytes per instruction; one
+  // head row per thread would touch 32 rows per instruction): latent dims
+  // 320..511 and the rope dims go straight into their swizzled shared-memory
+  // blocks, dims 0..319 into a row-major staging area in stage buffers 1..3
+  // (rows of 640 B, 16-byte chunks XOR-swizzled by row % 8), from which
+  // warps 4..11 move them into TMEM (q_first_tmem). Stage 0 is gathered
+  // meanwhile; stages 1..3 start once Q has left the staging area.
+  constexpr uint32_t kOffQStage = kOffK + kKStage;
+  auto q_first = [&](int item) {
+    constexpr int kTm = kUmHeads * (kQTmemDims / 8);  // 16-byte chunks of dims 0..319 (40 per row)
+    constexpr int kSm = kUmHeads * 32;                // chunks of dims 320..511 (24) and rope (8) per row
+    constexpr int kPerTm = (kTm + kThreadsQ - 1) / kThreadsQ;
+    const int t = (int)threadIdx.x - 32;
+    const size_t qrow0 = (size_t)make_item(p, item).token * kUmHeads;
+    const uint4* const qsrc = reinterpret_cast<const uint4*>(p.q + qrow0 * kDimLatent);
+    const uint4* const rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow0 * kDimRope);
+    // dims 320..511 and the rope dims: asynchronous copies into the swizzled blocks
+#pragma unroll 4
+    for (int j = t; j < kSm; j += kThreadsQ) {
+      const int r = j >> 5, c = j & 31;
+      const uint4* const src = c < 24 ? qsrc + r * 64 + 40 + c : rsrc + r * 8 + (c - 24);
+      const uint32_t dst = kOffQ + (uint32_t)(c >> 3) * kQBlock + (uint32_t)(r >> 3) * 1024u +
+                           (uint32_t)(r & 7) * 128u + (uint32_t)(((c & 7) ^ (r & 7)) * 16);
+      cp_async_16(base + dst, src);
+    }
     cp_async_commit();
-    uint32_t r[64];
+    // dims 0..319: registers, all loads in flight, then the staging area
+    uint4 v[kPerTm];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const uint4 v = __ldg(src + 24 + k);  // dims 192..319
-      r[4 * k] = v.x;
-      r[4 * k + 1] = v.y;
-      r[4 * k + 2] = v.z;
-      r[4 * k + 3] = v.w;
+    for (int i = 0; i < kPerTm; ++i) {
+      const int j = t + i * kThreadsQ;
+      if (j < kTm) v[i] = __ldg(qsrc + (j / 40) * 64 + (j % 40));
+    }
+#pragma unroll
+    for (int i = 0; i < kPerTm; ++i) {
+      const int j = t + i * kThreadsQ;
+      if (j < kTm) {
+        const int r = j / 40, c = j % 40;
+        *reinterpret_cast<uint4*>(sbase + kOffQStage + (uint32_t)r * 640u + (uint32_t)((c ^ (r & 7)) * 16)) = v[i];
+      }
+    }
+    cp_async_wait<0>();
+    fence_proxy_async_smem();  // the shared-memory Q blocks -> visible to the tensor core
+    named_bar_sync(1, kThreadsQ);
+  };
+  // Warps 4..11: dims 0..319 of the head rows of TMEM lane quadrant warp % 4
+  // from the staging area into TMEM; the issuer warp takes chunks 0..19,
+  // the softmax warp chunks 20..39 (16-byte chunk u -> TMEM columns 4u..4u+3).
+  auto q_first_tmem = [&]() {
+    const int row = (warp & 3) * 32 + lane;
+    const int c0 = warp >= kSoftWarp0 ? 20 : 0;
+    uint32_t r[80];
+#pragma unroll
+    for (int i = 0; i < 20; ++i) {
+      const uint4 x =
+          *reinterpret_cast<const uint4*>(sbase + kOffQStage + (uint32_t)row * 640u + (uint32_t)(((c0 + i) ^ (row & 7)) * 16));
+      r[4 * i] = x.x;
+      r[4 * i + 1] = x.y;
+      r[4 * i + 2] = x.z;
+      r[4 * i + 3] = x.w;
     }
     const uint32_t t_lane = (uint32_t)((warp & 3) * 32) << 16;
-    tmem_st32(tmem + t_lane + kTmemQ + 96, r);
-    tmem_st32(tmem + t_lane + kTmemQ + 128, r + 32);
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
+    const uint32_t col = tmem + t_lane + kTmemQ + (uint32_t)(4 * c0);
+    tmem_st32(col, r);
+    tmem_st32(col + 32, r + 32);
+    tmem_st16(col + 64, r + 64);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
+  };
+  auto q_help = [&](int item) {
+    q_first(item);
+    q_first_tmem();
     if (lane == 0) mbar_arrive(bar(kQHelp));
   };
 
@@ -585,12 +627,19 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     cursor_advance(p, n_items, nx2, kUmStages);
     int idx_cur = cursor_index(p, cur, lane);
     int idx_nx = cursor_index(p, nx, lane);
+    if (s > 0 && item0 < n_items) q_first(item0);
     uint32_t n = 0;  // tiles this warp filled
     bool ok = true;
     while (cur.item < n_items) {
       if (n > 0) {  // the stage's previous tile has been consumed by its PV
         if (lane == 0) ok = mbar_wait(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag, false, lim);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+      } else if (s > 0) {
+        // stages 1..3 hold the first item's Q staging area until warps 4..11
+        // have moved it into TMEM
+        ok = wait_warp(bar(kQFull), 0u, abort_flag, lim);
+        if (ok) ok = wait_warp(bar(kQHelp), 0u, abort_flag, lim);
         if (!ok) break;
       }
       const int row = checked_index(min(max(idx_cur, 0), L - 1), L, p.status);  // clamped address; masked below
@@ -731,6 +780,13 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const uint32_t* const mask_all = reinterpret_cast<const uint32_t*>(sbase + kOffMask);
     uint32_t g = 0, it = 0;
     bool ok = true;
+    // the first item's Q: the shared load of warps 1..11 (before any bounded
+    // wait, so every participant reaches its named barrier), then this
+    // warp's half of dims 0..319 into TMEM
+    if (item0 < n_items) {
+      q_first(item0);
+      q_first_tmem();
+    }
     for (int item = item0; item < n_items && ok; item += gridDim.x, ++it) {
       const Item w = make_item(p, item);
       if (it == 0 && p.wait_test != 0 && blockIdx.x == 0) {
@@ -744,46 +800,38 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
       // are complete (its epilogue waited for its last PV), and every QK
       // issuer has seen the previous item's Q.
       if (it > 0 && !(ok = wait_warp(bar(kQSeen), (it - 1) & 1u, abort_flag, lim))) break;
-      {
-        // the first item: latent dims 0..191 (TMEM) and 320..447 (shared
-        // memory) here, the rest by the issuer warps; later items: all of it
-        const bool first = it == 0;
+      if (it > 0) {
+        // later items: this thread's head row, dims 320..511 and the rope
+        // dims -> shared memory asynchronously, dims 0..319 -> TMEM in 64-dim
+        // chunks with three chunks' loads in flight
         const size_t qrow = (size_t)w.token * kUmHeads + row;
         const uint4* src = reinterpret_cast<const uint4*>(p.q + qrow * kDimLatent);
-        // dims 320..511 and the rope dims -> shared memory, asynchronously
         const uint32_t qdst = base + kOffQ + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u;
 #pragma unroll
         for (int k = 0; k < (kDimLatent - kQTmemDims) / 8; ++k)  // latent dims 320..511: 3 blocks
-          if (k < 16 || !first)
-            cp_async_16(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16), src + kQTmemDims / 8 + k);
-        if (!first) {
-          const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
+          cp_async_16(qdst + (k >> 3) * kQBlock + (((k & 7) ^ (row & 7)) * 16), src + kQTmemDims / 8 + k);
+        const uint4* rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow * kDimRope);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) cp_async_16(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16), rsrc + k);
-        }
+        for (int k = 0; k < 8; ++k) cp_async_16(qdst + 3 * kQBlock + ((k ^ (row & 7)) * 16), rsrc + k);
         cp_async_commit();
-        // dims 0..319 -> TMEM in 64-dim chunks, three chunks' loads in flight
-        const int nch = first ? 3 : kQTmemDims / 64;
         uint4 qa[24];
 #pragma unroll
         for (int k = 0; k < 24; ++k) qa[k] = __ldg(src + k);
 #pragma unroll
         for (int ch = 0; ch < kQTmemDims / 64; ++ch) {
-          if (ch < nch) {
-            uint32_t r[32];
+          uint32_t r[32];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint4 v = qa[(ch % 3) * 8 + k];
-              r[4 * k] = v.x;
-              r[4 * k + 1] = v.y;
-              r[4 * k + 2] = v.z;
-              r[4 * k + 3] = v.w;
-            }
-            tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
-            if (ch + 3 < nch) {
+          for (int k = 0; k < 8; ++k) {
+            const uint4 v = qa[(ch % 3) * 8 + k];
+            r[4 * k] = v.x;
+            r[4 * k + 1] = v.y;
+            r[4 * k + 2] = v.z;
+            r[4 * k + 3] = v.w;
+          }
+          tmem_st32(tmem + t_lane + kTmemQ + ch * 32, r);
+          if (ch + 3 < kQTmemDims / 64) {
 #pragma unroll
-              for (int k = 0; k < 8; ++k) qa[(ch % 3) * 8 + k] = __ldg(src + (ch + 3) * 8 + k);
-            }
+            for (int k = 0; k < 8; ++k) qa[(ch % 3) * 8 + k] = __ldg(src + (ch + 3) * 8 + k);
           }
         }
         cp_async_wait<0>();
@@ -791,8 +839,8 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kQFull));
       }
+      if (lane == 0) mbar_arrive(bar(kQFull));
       float m_true = kNegFltMax, m_used = kNegFltMax, l = 0.f;
       for (int t = 0; t < w.ntiles && ok; ++t, ++g) {
         const uint32_t s = g % kUmStages;
