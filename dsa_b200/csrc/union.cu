@@ -13,16 +13,21 @@
 // a block with no valid index gets one entry that no query selects.
 //
 // One CTA per block: counts per (key, query) for a range of kKeysPerPass
-// keys at a time in shared memory (16-bit, two queries per word), then a
-// block-wide exclusive scan of the per-key entry counts gives each key's
-// output position.
+// keys at a time in shared memory (16-bit, two queries per word), then one
+// block-wide exclusive scan per pass of the per-key entry counts (each thread
+// owns four consecutive keys) gives each key's output position. The block's
+// indices are read once into registers when they fit (16 per thread, two
+// 16-bit keys per register, for L < 65535) and reused by every pass.
 #include "dsa_common.cuh"
 
 namespace dsa {
 namespace {
 
 constexpr int kUnionThreads = 1024;
-constexpr int kKeysPerPass = 4096;
+constexpr int kKeysPerThread = 4;
+constexpr int kKeysPerPass = kUnionThreads * kKeysPerThread;  // 4096
+constexpr int kIdsCached = 16;                                // indices per thread kept in registers
+constexpr uint32_t kNoKey = 0xFFFFu;                          // a cached index that selects nothing
 
 // Counts of one key for QPB queries: QPB / 2 words, 16 bits per query.
 template <int QPB>
@@ -39,8 +44,33 @@ struct KeyCounts {
       w[0] = cnt[key];
     }
   }
-  __device__ __forceinline__ uint32_t of(int q) const { return (w[q >> 1] >> (16 * (q & 1))) & 0xFFFFu; }
+  // max over the queries' 16-bit counts (per-halfword maxima, then the halves)
+  __device__ __forceinline__ int max_count() const {
+    uint32_t v = w[0];
+#pragma unroll
+    for (int k = 1; k < QPB / 2; ++k) v = __vmaxu2(v, w[k]);
+    return (int)max(v & 0xFFFFu, v >> 16);
+  }
+  // membership bits of entry e: query q's bit is set when its count exceeds e
+  __device__ __forceinline__ uint32_t bits_above(uint32_t e) const {
+    const uint32_t ee = e | (e << 16);
+    uint32_t bits = 0;
+#pragma unroll
+    for (int k = 0; k < QPB / 2; ++k) {
+      const uint32_t gt = __vcmpgtu2(w[k], ee);  // 0xFFFF per halfword where count > e
+      bits |= ((gt & 1u) | ((gt >> 15) & 2u)) << (2 * k);
+    }
+    return bits;
+  }
 };
+
+// Count index slot j (query q = j / topk of the block) for key idx when it
+// lies in this pass's keys [k0, k1).
+template <int QPB>
+__device__ __forceinline__ void count_slot(uint32_t* cnt, int idx, int q, int k0, int k1) {
+  constexpr int kWords = QPB / 2;
+  if (idx >= k0 && idx < k1) atomicAdd(&cnt[(idx - k0) * kWords + (q >> 1)], 1u << (16 * (q & 1)));
+}
 
 template <int QPB>
 __global__ void __launch_bounds__(kUnionThreads, 2) union_build_kernel(const int32_t* __restrict__ ids, int topk,
@@ -48,70 +78,92 @@ __global__ void __launch_bounds__(kUnionThreads, 2) union_build_kernel(const int
                                                                      int32_t* __restrict__ ulen, int ucap) {
   constexpr int kWords = QPB / 2;
   extern __shared__ __align__(16) uint32_t cnt[];  // [kKeysPerPass][kWords]
-  __shared__ int warp_sums[2][kUnionThreads / 32];  // alternate chunks: two barriers per chunk
+  __shared__ int warp_sums[kUnionThreads / 32];
   const int blk = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int32_t* bids = ids + (size_t)blk * QPB * topk;  // the block's QPB index rows
   int32_t* bent = uent + (size_t)blk * ucap;
   const int n_ids = QPB * topk;
-  int base_out = 0;  // entries written before this chunk (the same in every thread)
-  int buf = 0;
+  const bool cached = n_ids <= kIdsCached * kUnionThreads && length < (int)kNoKey;
+  // cached path: thread tid holds slots tid / QPB + i * (1024 / QPB) of query
+  // tid % QPB, so its query needs no division
+  constexpr int kPerQuery = kUnionThreads / QPB;
+  const int cq = tid % QPB;
+  uint32_t idr[kIdsCached / 2];  // two 16-bit keys per register
+  if (cached) {
+#pragma unroll
+    for (int i = 0; i < kIdsCached; ++i) {
+      const int j = tid / QPB + i * kPerQuery;
+      const int idx = j < topk ? __ldg(bids + (size_t)cq * topk + j) : -1;
+      const uint32_t k = (idx >= 0 && idx < length) ? (uint32_t)idx : kNoKey;
+      if (i & 1)
+        idr[i >> 1] |= k << 16;
+      else
+        idr[i >> 1] = k;
+    }
+  }
+  int base_out = 0;  // entries written before this pass (the same in every thread)
   for (int k0 = 0; k0 < length; k0 += kKeysPerPass) {
-    for (int i = tid; i < kKeysPerPass * kWords; i += kUnionThreads) cnt[i] = 0u;
+    uint4* const c4 = reinterpret_cast<uint4*>(cnt);
+    for (int i = tid; i < kKeysPerPass * kWords / 4; i += kUnionThreads) c4[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
     const int k1 = min(length, k0 + kKeysPerPass);
+    if (cached) {
+#pragma unroll
+      for (int i = 0; i < kIdsCached; ++i)
+        count_slot<QPB>(cnt, (int)((idr[i >> 1] >> (16 * (i & 1))) & 0xFFFFu), cq, k0, k1);
+    } else {
 #pragma unroll 4
-    for (int i = tid; i < n_ids; i += kUnionThreads) {
-      const int idx = __ldg(bids + i);
-      if (idx >= k0 && idx < k1) {
-        const int q = i / topk;
-        atomicAdd(&cnt[(idx - k0) * kWords + (q >> 1)], 1u << (16 * (q & 1)));
-      }
+      for (int j = tid; j < n_ids; j += kUnionThreads) count_slot<QPB>(cnt, __ldg(bids + j), j / topk, k0, k1);
     }
     __syncthreads();
-    // keys of this pass in ascending order, kUnionThreads at a time
-    for (int kb = 0; kb < kKeysPerPass && k0 + kb < length; kb += kUnionThreads) {
-      const int key = kb + tid;
-      KeyCounts<QPB> c;
-      int m = 0;
+    // keys k0 + 4 tid .. 4 tid + 3 of this pass
+    int tot = 0;
+#pragma unroll
+    for (int i = 0; i < kKeysPerThread; ++i) {
+      const int key = kKeysPerThread * tid + i;
       if (k0 + key < length) {
+        KeyCounts<QPB> c;
         c.load(cnt, key);
-#pragma unroll
-        for (int q = 0; q < QPB; ++q) m = max(m, (int)c.of(q));
-      }
-      // block-wide exclusive scan of m
-      int incl = m;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
-      }
-      // warp_sums[buf] was last read two chunks ago, before the barriers of
-      // the previous chunk that every thread has passed
-      int* ws = warp_sums[buf];
-      if (lane == 31) ws[warp] = incl;
-      __syncthreads();
-      if (warp == 0) {
-        int s = ws[lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int v = __shfl_up_sync(0xffffffffu, s, o);
-          if (lane >= o) s += v;
-        }
-        ws[lane] = s;  // inclusive prefix over warps
-      }
-      __syncthreads();
-      const int pos = base_out + (warp > 0 ? ws[warp - 1] : 0) + incl - m;
-      base_out += ws[kUnionThreads / 32 - 1];
-      buf ^= 1;
-      for (int e = 0; e < m; ++e) {
-        uint32_t bits = 0;
-#pragma unroll
-        for (int q = 0; q < QPB; ++q) bits |= (c.of(q) > (uint32_t)e ? 1u : 0u) << q;
-        if (pos + e < ucap) bent[pos + e] = (int32_t)((uint32_t)(k0 + key) | (bits << 24));
+        tot += c.max_count();
       }
     }
-    __syncthreads();  // the next pass clears the counts
+    // block-wide exclusive scan of the threads' entry counts
+    int incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int sw = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, sw, o);
+        if (lane >= o) sw += v;
+      }
+      warp_sums[lane] = sw;  // inclusive prefix over warps
+    }
+    __syncthreads();
+    int pos = base_out + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - tot;
+    base_out += warp_sums[kUnionThreads / 32 - 1];
+#pragma unroll
+    for (int i = 0; i < kKeysPerThread; ++i) {
+      const int key = kKeysPerThread * tid + i;
+      if (k0 + key >= length) break;
+      KeyCounts<QPB> c;  // read again: fewer live registers across the scan
+      c.load(cnt, key);
+      const int mi = c.max_count();
+      for (int e = 0; e < mi; ++e) {
+        const uint32_t bits = c.bits_above((uint32_t)e);
+        if (pos + e < ucap)
+          bent[pos + e] = (int32_t)((uint32_t)(k0 + key) | (bits << 24));
+      }
+      pos += mi;
+    }
+    __syncthreads();  // the next pass clears the counts and reuses warp_sums
   }
   // a block whose queries have no valid index still gets one (fully masked)
   // entry, so that its item has a tile and writes zeros like any other row
