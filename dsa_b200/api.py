@@ -238,12 +238,12 @@ def _launch_records(launch, count):
     """Descriptors of the kernels one call enqueued, in launch order: the
     union build before the union launch's pair kernel; the split merge after
     a main kernel with split > 1, unless the main kernel merged its partials
-    itself (the split-V family's cluster merge: one kernel)."""
+    itself (the split-V and stream families' cluster merge: one kernel)."""
     name = "dsa_fwd_" + _FAMILY_NAMES.get(launch.family, str(launch.family))
     fields = (launch.family, launch.heads_per_cta, launch.keys_per_tile, launch.split)
     if launch.family == _native.FAMILY_PAIR_UNION:
         names = ["dsa_union_build", name]
-    elif launch.split > 1 and not (launch.family == _native.FAMILY_UMMA and count == 1):
+    elif launch.split > 1 and not (launch.family in (_native.FAMILY_UMMA, _native.FAMILY_STREAM) and count == 1):
         names = [name, "dsa_merge"]
     else:
         names = [name]

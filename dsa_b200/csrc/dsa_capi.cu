@@ -65,9 +65,18 @@ Layout partial_layout(int64_t tokens, int64_t heads, int64_t split, bool cluster
   return lay;
 }
 
-// Whether a launch entry merges its split partials inside the main kernel.
-bool merges_in_kernel(const dsa_launch_t& e) {
+// Whether a launch entry's partials take the split-V cluster merge's layout.
+bool umma_layout_merge(const dsa_launch_t& e) {
   return e.family == DSA_FAMILY_UMMA && e.split > 1 && dsa::umma_cluster_merge(e.split);
+}
+
+// Whether a launch entry merges its split partials inside the main kernel
+// (the split-V and stream families' cluster launches).
+bool merges_in_kernel(const dsa_launch_t& e) {
+  if (e.split <= 1) return false;
+  if (e.family == DSA_FAMILY_UMMA) return dsa::umma_cluster_merge(e.split);
+  if (e.family == DSA_FAMILY_STREAM) return dsa::stream_cluster_merge(e.split);
+  return false;
 }
 
 // Union launch: per block of 128 / H queries, up to (128 / H) * topk union
@@ -233,7 +242,7 @@ uint64_t dsa_fwd_workspace_bytes(const dsa_fwd_args_t* a) {
   if (dsa_check_launch(a->batch, a->queries, a->heads, a->length, a->topk, &e) != DSA_STATUS_OK)
     return 0;
   if (e.family == DSA_FAMILY_PAIR_UNION) return union_layout(a->batch * a->queries, a->heads, a->topk).total;
-  return partial_layout(a->batch * a->queries, a->heads, e.split, merges_in_kernel(e)).total;
+  return partial_layout(a->batch * a->queries, a->heads, e.split, umma_layout_merge(e)).total;
 }
 
 int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
@@ -255,7 +264,7 @@ int dsa_sparse_mla_fwd(const dsa_fwd_args_t* a, void* stream) {
 
   const int64_t tokens = a->batch * a->queries;
   const bool fused_merge = merges_in_kernel(e);
-  const Layout lay = partial_layout(tokens, a->heads, e.split, fused_merge);
+  const Layout lay = partial_layout(tokens, a->heads, e.split, umma_layout_merge(e));
   if (e.family == DSA_FAMILY_PAIR_UNION) {
     const UnionLayout ul = union_layout(tokens, a->heads, a->topk);
     if (a->workspace == nullptr || a->workspace_bytes < ul.total ||

@@ -216,6 +216,7 @@ cudaError_t launch_union_build(const int32_t* ids, int topk, int length, int qpb
                                int32_t* ulen, int ucap, cudaStream_t stream);
 // CTAs of the stream family resident at once (-1 on error).
 int stream_max_ctas();
+bool stream_cluster_merge(int split);
 int keys_max_ctas();
 cudaError_t launch_paged_rows(const int32_t* ids, const int32_t* block_table, const int32_t* seq_lens, int32_t* rows,
                               long long n, int per_batch, int max_blocks, int block_size, int num_blocks,

@@ -118,6 +118,85 @@ __device__ __forceinline__ void compute_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(32 * kStComputeWarps) : "memory");
 }
 
+// Split merge inside the cluster-merge launch: the `split` CTAs of one
+// (token, 16-head group) form a cluster, one item each, and after their
+// partials (dsa/api.py:111-113 layout) are in the L2 and one cluster
+// barrier, CTA rank r merges heads [16 r / S, 16 (r + 1) / S) of the group:
+// the merge of dsa/merge.py:13-91 (as merge_kernel: M = max m_s,
+// w_s = exp(m_s - M), L = sum w_s l_s, O = sum w_s u_s / L, splits in
+// order), one warp per head row, lane i owning columns 4i + 128j. Every
+// thread of every CTA takes the barrier, also after a failed wait (it then
+// skips the work).
+__device__ __forceinline__ void stream_cluster_merge(const FwdParams& p, bool live) {
+  cluster_sync();  // every split's partials of the cluster are in the L2
+  if (!live) return;
+  const int S = p.split;
+  const int item = (int)blockIdx.x;
+  const int sp = item % S;
+  const int rest = item / S;
+  const int hgroups = p.heads / kStHeads;
+  const int hg = rest % hgroups, token = rest / hgroups;
+  const int r0 = sp * kStHeads / S, r1 = (sp + 1) * kStHeads / S;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = r0 + warp; r < r1; r += kStThreads / 32) {
+    const int h = hg * kStHeads + r;
+    const size_t stat0 = (size_t)token * S * p.heads + h;  // + s * heads
+    const float ms = lane < S ? __ldcg(p.part_max + stat0 + (size_t)lane * p.heads) : -INFINITY;
+    const float ls = lane < S ? __ldcg(p.part_sum + stat0 + (size_t)lane * p.heads) : 0.f;
+    float m = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float ws = lane < S ? expf(ms - m) : 0.f;
+    float l = ws * ls;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    float4 u[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) u[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < S; s0 += 4) {  // four splits' rows in flight
+      float4 v[4][4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        if (s0 + b < S) {
+          const float4* row =
+              reinterpret_cast<const float4*>(p.part_num + (stat0 + (size_t)(s0 + b) * p.heads) * kDimLatent) + lane;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[b][j] = __ldcg(row + 32 * j);
+        }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const float wb = __shfl_sync(0xffffffffu, ws, (s0 + b) & 31);
+        if (s0 + b < S) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            u[j].x += wb * v[b][j].x;
+            u[j].y += wb * v[b][j].y;
+            u[j].z += wb * v[b][j].z;
+            u[j].w += wb * v[b][j].w;
+          }
+        }
+      }
+    }
+    const float ld = l > 0.f ? l : INFINITY;  // no valid index in any split: output 0
+    __nv_bfloat16* const orow = p.out + ((size_t)token * p.heads + h) * kDimLatent;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint2 packed;
+      packed.x = pack_bf16x2(__fdiv_rn(u[j].x, ld), __fdiv_rn(u[j].y, ld));
+      packed.y = pack_bf16x2(__fdiv_rn(u[j].z, ld), __fdiv_rn(u[j].w, ld));
+      *reinterpret_cast<uint2*>(orow + 4 * lane + 128 * j) = packed;
+    }
+    if (lane == 0) {
+      p.out_max[(size_t)token * p.heads + h] = l > 0.f ? m : -INFINITY;
+      p.out_sum[(size_t)token * p.heads + h] = l;
+    }
+  }
+}
+
+// kCM: the cluster-merge launch (one item per CTA, the split CTAs of a
+// (token, head group) as one cluster, stream_cluster_merge at the end);
+// otherwise persistent CTAs and merge_kernel for split > 1.
+template <bool kCM>
 __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StSmem& sm = *reinterpret_cast<StSmem*>(smem_raw);
@@ -191,6 +270,7 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
       idx_nx = idx_nx2;
     }
     if (!ok && lane == 0) report_error(p.status, kErrTimeout);
+    if constexpr (kCM) stream_cluster_merge(p, !(*abort_flag) && !*reinterpret_cast<volatile int*>(&sm.stop));
     return;
   }
 
@@ -395,6 +475,7 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
     }
   }
   if (failed && ctid == 0) report_error(p.status, kErrTimeout);
+  if constexpr (kCM) stream_cluster_merge(p, !(*abort_flag) && !*reinterpret_cast<volatile int*>(&sm.stop));
 }
 
 }  // namespace
@@ -403,10 +484,12 @@ int stream_max_ctas() {
   static int cached = -1;
   if (cached > 0) return cached;
   const int smem = (int)sizeof(StSmem);
-  if (cudaFuncSetAttribute(fwd_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  if (cudaFuncSetAttribute(fwd_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
     return -1;
   int per_sm = 0, dev = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_stream_kernel, kStThreads, smem) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_stream_kernel<false>, kStThreads, smem) !=
+          cudaSuccess ||
       per_sm <= 0)
     return -1;
   if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -416,14 +499,69 @@ int stream_max_ctas() {
   return cached;
 }
 
+namespace {
+
+constexpr int kStMaxClusterSplit = 8;  // portable cluster sizes only
+
+void st_cm_launch_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, int split, long long ctas,
+                         cudaStream_t stream) {
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = (unsigned)split;
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
+  *cfg = cudaLaunchConfig_t{};
+  cfg->gridDim = dim3((unsigned)ctas, 1, 1);
+  cfg->blockDim = dim3(kStThreads, 1, 1);
+  cfg->dynamicSmemBytes = sizeof(StSmem);
+  cfg->stream = stream;
+  cfg->attrs = attr;
+  cfg->numAttrs = 1;
+}
+
+}  // namespace
+
+// Whether the stream family merges `split` partials in its cluster launch:
+// a portable cluster size whose clusters fit on the GPU (they may run in
+// waves: clusters do not wait on one another).
+bool stream_cluster_merge(int split) {
+  static int cached[kStMaxClusterSplit + 1];
+  static bool init = false;
+  if (split < 2 || split > kStMaxClusterSplit) return false;
+  if (!init) {
+    if (cudaFuncSetAttribute(fwd_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(StSmem)) != cudaSuccess)
+      return false;
+    for (int k = 0; k <= kStMaxClusterSplit; ++k) cached[k] = -1;
+    init = true;
+  }
+  if (cached[split] < 0) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    st_cm_launch_config(&cfg, &attr, split, split, nullptr);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fwd_stream_kernel<true>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cached[split] = n;
+  }
+  return cached[split] > 0;
+}
+
 cudaError_t launch_fwd_stream(const FwdParams& p, cudaStream_t stream) {
   if (p.heads % kStHeads != 0 || p.keys_per_tile != kStBN) return cudaErrorInvalidValue;
-  const int max_ctas = stream_max_ctas();
-  if (max_ctas <= 0) return cudaErrorInvalidConfiguration;
   const long long items = (long long)p.tokens * (p.heads / kStHeads) * p.split;
   if (items <= 0 || items > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  if (p.split > 1 && stream_cluster_merge(p.split)) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    st_cm_launch_config(&cfg, &attr, p.split, items, stream);
+    return cudaLaunchKernelEx(&cfg, fwd_stream_kernel<true>, p);
+  }
+  const int max_ctas = stream_max_ctas();
+  if (max_ctas <= 0) return cudaErrorInvalidConfiguration;
   const int ctas = (int)(items < max_ctas ? items : max_ctas);
-  fwd_stream_kernel<<<ctas, kStThreads, sizeof(StSmem), stream>>>(p);
+  fwd_stream_kernel<false><<<ctas, kStThreads, sizeof(StSmem), stream>>>(p);
   return cudaGetLastError();
 }
 
