@@ -65,17 +65,15 @@ TRAFFIC_MODEL = {
     # 32.2 MB read + 0.17 MB written, of which the 9.4 MB kv + k_rope is
     # read once (it stays L2-resident) and the rest scales with the queries.
     "prefill_tp8": (9.4e6, (32.2e6 - 9.4e6 + 0.17e6) / 1024),
-    # fwd_stream_kernel, capture of 64 queries x 2048 keys at L = 16384 (the
-    # same gathered rows per launch as decode_tp8; only L differs):
-    # 152.8 MB read + 3.8 MB written.
-    "decode_tp8": (0.0, (152.8e6 + 3.8e6) / 64),
-    # fwd_umma_kernel (cluster merge), capture of 18 full decode_b8 launches:
-    # 39.07 MB read + 0.07 MB written (the FP32 partials stay in the L2).
-    "decode_b8": (0.0, (39.07e6 + 0.07e6) / 16),
-    # fwd_umma_kernel, capture of a full decode_b1 launch with split 32 and
-    # a separate merge (before the cluster merge; the DRAM reads are the
-    # gathered rows and Q either way): 2,586,368 B read.
-    "decode_b1": (0.0, 2586368.0),
+    # fwd_stream_kernel (cluster merge), capture of ten full decode_tp8
+    # launches: 152.8 MB read + 0.48 MB written.
+    "decode_tp8": (0.0, (152.8e6 + 0.48e6) / 64),
+    # fwd_umma_kernel (cluster merge), capture of ten full decode_b8 launches:
+    # 39.10 MB read + 0.06 MB written (the FP32 partials stay in the L2).
+    "decode_b8": (0.0, (39.10e6 + 0.06e6) / 16),
+    # fwd_umma_kernel (cluster merge, split 16), capture of ten full
+    # decode_b1 launches: 2.62 MB read, nothing written back to DRAM.
+    "decode_b1": (0.0, 2.62e6),
 }
 
 
