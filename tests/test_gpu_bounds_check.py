@@ -20,7 +20,8 @@ CASES = [  # (shape, Tuning args or None, index family)
     ((1, 1, 128, 4096, 2048), (128, 32, 32, 256), "invalid"),  # split-V + merge kernel
     ((1, 80, 128, 4096, 256), (128, 32, 1, 512), "normal"),    # pair
     ((1, 64, 16, 1024, 256), (16, 32, 1, 128), "invalid"),     # union + pair
-    ((4, 1, 16, 8192, 2048), (16, 32, 8, 512), "duplicates"),  # stream + merge
+    ((4, 1, 16, 8192, 2048), (16, 32, 8, 512), "duplicates"),  # stream, cluster merge
+    ((4, 1, 16, 8192, 2048), (16, 32, 16, 512), "invalid"),    # stream + merge kernel
     ((2, 2, 32, 4096, 512), (16, 64, 2, 128), "normal"),       # keys
     ((2, 2, 32, 4096, 512), (16, 64, 3, 512), "invalid"),      # warp-MMA + merge
 ]

@@ -1,11 +1,15 @@
-"""The split-V family's merge inside the kernel (one launch per call).
+"""Split merges inside the main kernel (one launch per call).
 
-With split S in 2..16 the S CTAs of one (token, value half) run as one
-thread-block cluster and merge their FP32 partials themselves (the merge of
-dsa/merge.py:13-91: m = max m_s, w_s = exp(m_s - m), l = sum w_s l_s,
-O = sum w_s O_s / l) through the L2 and two cluster barriers, so no separate
-merge kernel runs. Checked against the CPU oracle with the parity gates,
-including splits whose keys are all masked and rows without a valid index.
+Split-V family, split S in 2..16: the S CTAs of one (token, value half) run
+as one thread-block cluster and merge their FP32 partials themselves (the
+merge of dsa/merge.py:13-91: m = max m_s, w_s = exp(m_s - m),
+l = sum w_s l_s, O = sum w_s O_s / l): partials through the L2, row
+statistics through distributed shared memory when S divides 128 (else the
+L2), one cluster barrier. Stream family, split 2..8: the split CTAs of one
+(token, 16-head group) form the cluster and merge the same way after one
+cluster barrier. No separate merge kernel runs. Checked against the CPU
+oracle with the parity gates, including splits whose keys are all masked and
+rows without a valid index.
 """
 import pytest
 import torch
@@ -93,3 +97,26 @@ def test_default_decode_launch_is_one_kernel(cuda_lib):
         _, kernels = dsa_b200.forward(*data, return_kernels=True)
         torch.cuda.synchronize()
         assert [k.name for k in kernels] == ["dsa_fwd_umma"], (name, kernels)
+
+
+@pytest.mark.parametrize("split", [2, 3, 4, 8])
+def test_stream_cluster_merge(cuda_lib, split):
+    """The stream family (16-head groups) with splits 2..8: one kernel, the
+    reference's "invalid" family (splits without a valid key) and a query
+    without any valid index (output 0, max -inf, sum 0)."""
+    shape = (2, 2, 32, 4096, 1024)
+    q, kv, qr, kr, ids = oracle.make_inputs(shape, 20261104, "invalid")
+    ids[1, 0] = -1
+    data = (q, kv, qr, kr, ids)
+    (out, mx, sm), kernels = dsa_b200.forward(*[t.cuda() for t in data], config=dsa_b200.Tuning(16, 32, split),
+                                              return_kernels=True)
+    torch.cuda.synchronize()
+    assert dsa_b200.device_status() == 0
+    assert [k.name for k in kernels] == ["dsa_fwd_stream"], kernels
+    ref = oracle.reference_forward(*data, defined_invalid=True)
+    out, mx, sm = out.float().cpu(), mx.cpu(), sm.cpu()
+    assert torch.equal(out[1, 0], torch.zeros_like(out[1, 0]))
+    assert bool(torch.isneginf(mx[1, 0, 0]).all()) and torch.equal(sm[1, 0, 0], torch.zeros_like(sm[1, 0, 0]))
+    for b, t in ((0, 0), (0, 1), (1, 1)):
+        _check((out[b:b + 1, t:t + 1], mx[b:b + 1, :, t:t + 1], sm[b:b + 1, :, t:t + 1]),
+               (ref[0][b:b + 1, t:t + 1], ref[1][b:b + 1, :, t:t + 1], ref[2][b:b + 1, :, t:t + 1]))
