@@ -55,7 +55,7 @@ constexpr int kPvWarp = kQkWarp0 + kQkIssuers;          // 7
 constexpr int kSoftWarp0 = kPvWarp + 1;                 // 8
 constexpr int kSoftWarps = 4;
 constexpr int kUmThreads = 32 * (kSoftWarp0 + kSoftWarps);  // 384
-constexpr int kThreadsQ = kUmThreads - 32;                   // warps 1..11 load the first item's Q
+constexpr int kThreadsQ = kUmThreads - 64;                   // warps 2..11 load the first item's Q
 constexpr int kUmHeads = 128;
 constexpr int kQTmemDims = 320;    // Q dims kept in TMEM (A operand of TS steps)
 constexpr int kQkSteps = kDimQK / 16;        // 36
@@ -533,20 +533,23 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     return true;
   };
 
-  // The first item's Q, loaded by warps 1..11 together with coalesced
+  // The first item's Q, loaded by warps 2..11 together with coalesced
   // 16-byte loads (a warp reads 512 contiguous bytes per instruction; one
   // head row per thread would touch 32 rows per instruction): latent dims
   // 320..511 and the rope dims go straight into their swizzled shared-memory
-  // blocks, dims 0..319 into a row-major staging area in stage buffers 1..3
-  // (rows of 640 B, 16-byte chunks XOR-swizzled by row % 8), from which
-  // warps 4..11 move them into TMEM (q_first_tmem). Stage 0 is gathered
-  // meanwhile; stages 1..3 start once Q has left the staging area.
-  constexpr uint32_t kOffQStage = kOffK + kKStage;
+  // blocks, dims 0..319 into a row-major staging area over stage buffers
+  // 2..3 and the P buffers (rows of 640 B, 16-byte chunks XOR-swizzled by
+  // row % 8), from which warps 4..11 move them into TMEM (q_first_tmem).
+  // Stages 0 and 1 are gathered meanwhile; stages 2..3 start once Q has left
+  // the staging area (the first P is written after the first scores, which
+  // need all of Q in TMEM).
+  constexpr uint32_t kOffQStage = kOffK + 2u * kKStage;
+  static_assert(kOffQStage + (uint32_t)kUmHeads * 640u <= kOffP + 2u * kPBytes, "Q staging area");
   auto q_first = [&](int item) {
     constexpr int kTm = kUmHeads * (kQTmemDims / 8);  // 16-byte chunks of dims 0..319 (40 per row)
     constexpr int kSm = kUmHeads * 32;                // chunks of dims 320..511 (24) and rope (8) per row
     constexpr int kPerTm = (kTm + kThreadsQ - 1) / kThreadsQ;
-    const int t = (int)threadIdx.x - 32;
+    const int t = (int)threadIdx.x - 64;
     const size_t qrow0 = (size_t)make_item(p, item).token * kUmHeads;
     const uint4* const qsrc = reinterpret_cast<const uint4*>(p.q + qrow0 * kDimLatent);
     const uint4* const rsrc = reinterpret_cast<const uint4*>(p.q_rope + qrow0 * kDimRope);
@@ -627,7 +630,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     cursor_advance(p, n_items, nx2, kUmStages);
     int idx_cur = cursor_index(p, cur, lane);
     int idx_nx = cursor_index(p, nx, lane);
-    if (s > 0 && item0 < n_items) q_first(item0);
+    if (s > 1 && item0 < n_items) q_first(item0);
     uint32_t n = 0;  // tiles this warp filled
     bool ok = true;
     while (cur.item < n_items) {
@@ -635,8 +638,8 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
         if (lane == 0) ok = mbar_wait(bar(kEmpty0 + s), (n - 1) & 1u, abort_flag, false, lim);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
-      } else if (s > 0) {
-        // stages 1..3 hold the first item's Q staging area until warps 4..11
+      } else if (s > 1) {
+        // stages 2..3 hold the first item's Q staging area until warps 4..11
         // have moved it into TMEM
         ok = wait_warp(bar(kQFull), 0u, abort_flag, lim);
         if (ok) ok = wait_warp(bar(kQHelp), 0u, abort_flag, lim);
@@ -780,7 +783,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) fwd_umma_kernel(const FwdParams
     const uint32_t* const mask_all = reinterpret_cast<const uint32_t*>(sbase + kOffMask);
     uint32_t g = 0, it = 0;
     bool ok = true;
-    // the first item's Q: the shared load of warps 1..11 (before any bounded
+    // the first item's Q: the shared load of warps 2..11 (before any bounded
     // wait, so every participant reaches its named barrier), then this
     // warp's half of dims 0..319 into TMEM
     if (item0 < n_items) {
