@@ -79,7 +79,10 @@ CASE_SHAPES = {
 }
 
 # Tuned entries per named shape. Shapes absent here use the library heuristic
-# (dsa_default_launch in dsa_b200/csrc/dsa_capi.cu).
+# (dsa_default_launch in dsa_b200/csrc/dsa_capi.cu). `python -m dsa_b200.tune`
+# measures every applicable entry against the heuristic; on B200 the
+# heuristic is the best entry (within 3 %) for every named shape, so the
+# table is empty.
 SELECTED: dict = {}
 
 _BY_SHAPE = {}

@@ -171,10 +171,17 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
   if (heads == 128) {
     e.heads_per_cta = 128;
     e.keys_per_tile = 32;
+    int ctas = dsa::umma_max_ctas();
+    if (ctas <= 0) ctas = sm_count();
+    const int64_t halves = 2 * batch * queries;
+    const int64_t tiles = (topk + 31) / 32;
     const int pair_ctas = dsa::pair_max_ctas();
-    if (pair_ctas > 0 && batch * queries >= pair_ctas / 2) {
-      // pair family: one (score CTA, value CTA) cluster per query; enough
-      // queries to occupy every cluster without splitting the TOPK range.
+    if (pair_ctas > 0 && ctas / halves < 2) {
+      // pair family: one (score CTA, value CTA) cluster per query, once the
+      // split-V family could no longer split the TOPK range (a pair's tile
+      // costs ~0.6 us against ~1 us for a split-V CTA, which also computes
+      // QK twice); measured on B200: 64 queries 65.5 us against 82.0 us,
+      // 32 queries (split-V split 2) 53 us and no faster as pairs.
       e.family = DSA_FAMILY_UMMA_PAIR;
       e.split = 1;
       *out = e;
@@ -184,10 +191,6 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
     // V half) items; split the TOPK range only until every resident CTA has
     // an item.
     e.family = DSA_FAMILY_UMMA;
-    int ctas = dsa::umma_max_ctas();
-    if (ctas <= 0) ctas = sm_count();
-    const int64_t halves = 2 * batch * queries;
-    const int64_t tiles = (topk + 31) / 32;
     int64_t split = ctas / halves;  // one wave: at most one item per resident CTA
     // at least two tiles per item: a one-tile item is all start-up (Q load,
     // first gather, epilogue) and doubles the partials the merge reads
@@ -200,14 +203,20 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
     *out = e;
     return DSA_STATUS_OK;
   }
-  // union launch of the pair family for 16 heads: blocks of 8 queries of one
-  // batch row over the union of their keys, when the blocks fill the
-  // clusters and the keys are dense enough (L <= 4 TOPK: the union of 8
-  // queries' keys is then at most ~3.6 TOPK, against 8 TOPK key-rows for the
-  // per-query form)
-  if (heads == 16 && queries % 8 == 0 && length <= 4 * topk && length < (1 << 24) && topk <= kUnionMaxTopk) {
+  // union launch of the pair family for 16, 32 or 64 heads: blocks of
+  // 128 / H queries of one batch row over the union of their keys, when the
+  // blocks fill the clusters and the keys are dense enough that the MMA work
+  // (128 rows x the union) stays within ~4x the per-query work, which the
+  // tcgen05 pair kernel still beats the mma.sync stream family at: L <= 4
+  // TOPK (8 queries' union ~3.6 TOPK for H = 16, 4 queries' ~2.7 TOPK for
+  // H = 32), any L for H = 64 (a 2-query union is at most 2 TOPK). Measured
+  // on B200 (B=4, SQ=8192, L=8192, TOPK=2048): H = 64 18.8 ms against 46.6 ms,
+  // H = 32 14.6 ms against 23.3 ms for the stream family.
+  const bool dense = heads == 64 || length <= 4 * topk;
+  if ((heads == 16 || heads == 32 || heads == 64) && queries % (128 / heads) == 0 && dense &&
+      length < (1 << 24) && topk <= kUnionMaxTopk) {
     const int pair_ctas = dsa::pair_max_ctas();
-    if (pair_ctas > 0 && batch * queries / 8 >= pair_ctas / 2) {
+    if (pair_ctas > 0 && batch * queries / (128 / heads) >= pair_ctas / 2) {
       e.family = DSA_FAMILY_PAIR_UNION;
       e.heads_per_cta = 128;
       e.keys_per_tile = 32;
@@ -227,6 +236,10 @@ int dsa_default_launch(int64_t batch, int64_t queries, int64_t heads, int64_t le
   const int64_t tiles = (topk + e.keys_per_tile - 1) / e.keys_per_tile;
   int64_t split = ctas / jobs;  // one wave of items
   if (split > tiles) split = tiles;
+  // with four or more jobs, at most the eight splits that merge inside the
+  // cluster launch (one kernel; measured faster than more splits and the
+  // merge kernel for 4-8 jobs: 22.5-22.6 us against 23.6-25.6 us)
+  if (jobs >= 4 && split > 8) split = 8;
   if (split < 1) split = 1;
   e.split = (int32_t)split;
   *out = e;

@@ -105,3 +105,24 @@ def test_union_prefill_tp8(cuda_lib):
            mx.reshape(b * s, h)[rows_t].reshape(len(rows), 1, 1, h),
            sm.reshape(b * s, h)[rows_t].reshape(len(rows), 1, 1, h))
     _check(got, ref)
+
+
+@pytest.mark.parametrize("name", ["prefill_b4_h64", "prefill_b4_h32"])
+def test_default_union_launch_for_32_and_64_heads(cuda_lib, name):
+    """The shape heuristic runs dense 32- and 64-head prefill (B=4,
+    SQ=8192, L=8192, TOPK=2048) on the union launch; sampled rows against
+    the oracle."""
+    shape = dsa_b200.CASE_SHAPES[name]
+    data = bench.make_device_inputs(shape, bench.SEED, "uniform", "cuda")
+    (out, mx, sm), kernels = dsa_b200.forward(*data, return_kernels=True)
+    torch.cuda.synchronize()
+    assert dsa_b200.device_status() == 0
+    assert [k.name for k in kernels] == ["dsa_union_build", "dsa_fwd_pair_union"], kernels
+    b, s, h, _, _ = shape
+    rows = list(range(0, b * s, 331)) + [b * s - 1]
+    ref = oracle.reference_forward(*bench.compact_for_oracle(data, rows))
+    rows_t = torch.as_tensor(rows, device="cuda")
+    got = (out.reshape(b * s, h, 512)[rows_t].unsqueeze(1),
+           mx.reshape(b * s, h)[rows_t].reshape(len(rows), 1, 1, h),
+           sm.reshape(b * s, h)[rows_t].reshape(len(rows), 1, 1, h))
+    _check(got, ref)
