@@ -78,7 +78,7 @@ def time_entry(data, tuning, reps, flush):
     return statistics.median(times)
 
 
-def tune(names, reps=20, margin=0.03, seed=20261103):
+def tune(names, reps=20, margin=0.03, seed=20261103, verbose=False):
     """{name: (heuristic µs, best Tuning or None, best µs)} for ``names``."""
     saved = dict(config.SELECTED)
     config.SELECTED.clear()
@@ -95,6 +95,8 @@ def tune(names, reps=20, margin=0.03, seed=20261103):
             best, best_us = None, base
             for t in candidates(shape):
                 us = time_entry(data, t, reps, flush)
+                if verbose:
+                    print(f"    {t}: {'not applicable' if us is None else f'{us:.1f} us'}", flush=True)
                 if us is not None and us < best_us * (1.0 - margin):
                     best, best_us = t, us
             results[name] = (base, best, best_us)
@@ -114,9 +116,10 @@ def main():
     ap.add_argument("--names", default=None, help="comma-separated CASE_SHAPES names (default: all)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--margin", type=float, default=0.03)
+    ap.add_argument("--verbose", action="store_true", help="print every candidate's time")
     args = ap.parse_args()
     names = args.names.split(",") if args.names else list(config.CASE_SHAPES)
-    results = tune(names, args.reps, args.margin)
+    results = tune(names, args.reps, args.margin, verbose=args.verbose)
     print("SELECTED = {")
     for name, (_, best, _) in results.items():
         if best is not None:
