@@ -409,19 +409,34 @@ __device__ __forceinline__ void merged_epilogue(const FwdParams& p, uint8_t* sba
   if (!live) return;
   // weights w_s / L of the owned rows -> the (free) P buffers [row - r0][16]
   float* const wts = reinterpret_cast<float*>(sbase + kOffP);
-  if (threadIdx.x < (unsigned)nrows) {
+  if (even) {
+    // one thread per (row, split) in groups of S lanes of a warp (S divides
+    // 32): the max and the sum are shuffle reductions over the group
+    const int t = (int)threadIdx.x;
+    if (t < nrows * S) {  // nrows * S == 128: warps 0..3, every lane
+      const int lr = t / S, k = t % S;
+      const float2 ms = sstat[k * nrows + lr];
+      float M = ms.x;
+      for (int o = 1; o < S; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      // an all-masked split (l = 0, O = 0) and a row without any valid index
+      // (L = 0: output 0) contribute nothing
+      const float e = ms.y > 0.f ? ex2((ms.x - M) * c) : 0.f;
+      float L = ms.y * e;
+      for (int o = 1; o < S; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+      wts[lr * 16 + k] = L > 0.f ? e * (1.f / L) : 0.f;
+      if (k == 0 && half == 0) {
+        const size_t orow = (size_t)token * kUmHeads + r0 + lr;
+        p.out_max[orow] = final_max(M, L, p.scale_div);
+        p.out_sum[orow] = L;
+      }
+    }
+  } else if (threadIdx.x < (unsigned)nrows) {
     const int lr = (int)threadIdx.x;
     const int row = r0 + lr;
     float2 ms[16];
-    if (even) {  // pushed into this CTA's shared memory
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (k < S) ms[k] = sstat[k * nrows + lr];
-    } else {
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (k < S) ms[k] = __ldcg(pstat + (size_t)k * kUmHeads + row);
-    }
+    for (int k = 0; k < 16; ++k)
+      if (k < S) ms[k] = __ldcg(pstat + (size_t)k * kUmHeads + row);
     float M = kNegFltMax;
 #pragma unroll
     for (int k = 0; k < 16; ++k)
