@@ -5,10 +5,15 @@
 // TP8): the math per row is small, so the kernel is bound by how many
 // gathered bytes are in flight (decode, rows from HBM) or by the L2 gather
 // rate (prefill with an L2-resident KV). Each CTA loops over work items
-// (token, 16-head group, KV split); two gather warps keep its two stages of
-// 32 rows x 1152 B in flight with 16-byte cp.async (validity taken from the
-// original index, dsa/workspace.py:121-128), independently of the compute
-// warps, and two CTAs share an SM.
+// (token, 16-head group, KV split). Gathered rows land in a ring of 16-row
+// units (a 32-key tile is two units): two gather warps, one per tile half,
+// fill the units with 16-byte cp.async (validity taken from the original
+// index, dsa/workspace.py:121-128) that complete on the unit's mbarrier, so
+// a warp runs ahead of the compute warps as far as the ring allows; two CTAs
+// share an SM. The ring has four units in the stage buffers plus, in the
+// cluster-merge launch (one item per CTA), a fifth in the Q buffer once the
+// compute warps hold Q in registers: 2.5 tiles of rows in flight instead of
+// two, which is what bounds the tile rate when the rows come from HBM.
 //
 // The four compute warps run the reference's per-tile dataflow
 // (dsa/workspace.py:242-318) with warp-level m16n8k16 BF16 MMAs: S = Q.K^T
@@ -35,8 +40,10 @@ using namespace umma;
 
 constexpr int kStHeads = 16;
 constexpr int kStBN = 32;
-constexpr int kStStages = 2;
-constexpr int kStGatherWarps = kStStages;  // gather warp w owns stage w
+constexpr int kStStages = 2;             // 32-row stage buffers (four 16-row units)
+constexpr int kStUnitRows = 16;          // rows per ring unit (one half of a tile)
+constexpr int kStGatherWarps = 2;        // gather warp w fills rows 16w..16w+15 of every tile
+constexpr int kStMaxUnits = 2 * kStStages + 1;  // the fifth unit is the Q buffer (cluster-merge launch)
 constexpr int kStComputeWarps = 4;
 constexpr int kStThreads = 32 * (kStGatherWarps + kStComputeWarps);
 constexpr int kStRow = kDimQK + 8;       // padded smem row (elements): 1168 B, odd multiple of 16 B
@@ -49,15 +56,30 @@ struct StSmem {
   __nv_bfloat16 k[kStStages][kStBN * kStRow];
   __nv_bfloat16 p[kStHeads * kStPRow];
   float s[kStComputeWarps][kStHeads * kStBN];  // partial scores of each compute warp's dims
-  int ids[kStStages][kStBN];
+  int ids[kStMaxUnits][kStUnitRows];
   float m[kStHeads];
   float l[kStHeads];
   float alpha[kStHeads];
-  unsigned long long full[kStStages];
-  unsigned long long empty[kStStages];
+  unsigned long long full[kStMaxUnits];   // unit gathered (32 cp.async arrivals, one per gather lane)
+  unsigned long long empty[kStMaxUnits];  // unit consumed (the four compute warps)
   int abort;
   int stop;  // a compute warp's bounded wait gave up: all compute warps leave
 };
+
+constexpr uint32_t kStUnitBytes = (uint32_t)(kStUnitRows * kStRow * 2);
+static_assert(sizeof(StSmem::q) == kStUnitBytes, "the Q buffer doubles as one ring unit");
+static_assert(sizeof(StSmem::k) == 2 * kStStages * kStUnitBytes, "the stage buffers hold four ring units");
+
+// Ring units of a launch: the Q buffer is the fifth unit only when every CTA
+// runs one item (its Q is loaded once, into registers).
+template <bool kCM>
+constexpr uint32_t st_units() {
+  return kCM ? (uint32_t)kStMaxUnits : (uint32_t)(2 * kStStages);
+}
+
+__device__ __forceinline__ uint32_t st_unit_addr(const StSmem& sm, uint32_t u) {
+  return u < (uint32_t)(2 * kStStages) ? smem_u32(sm.k) + u * kStUnitBytes : smem_u32(sm.q);
+}
 
 struct StItem {
   int token, hg, sp, batch, kbeg, kend, ntiles;
@@ -210,9 +232,9 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
   const uint32_t empty0 = smem_u32(&sm.empty[0]);
 
   if (tid == 0) {
-    for (int s = 0; s < kStStages; ++s) {
-      mbar_init(full0 + 8u * s, 1);
-      mbar_init(empty0 + 8u * s, kStComputeWarps);
+    for (int u = 0; u < kStMaxUnits; ++u) {
+      mbar_init(full0 + 8u * u, 32);  // one cp.async arrival per gather lane
+      mbar_init(empty0 + 8u * u, kStComputeWarps);
     }
     sm.abort = 0;
     sm.stop = 0;
@@ -220,55 +242,59 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
   }
   __syncthreads();
 
+  constexpr uint32_t kUnits = st_units<kCM>();
   if (warp < kStGatherWarps) {
-    // ---------------- gather: warp w fills stage w for tiles w, w + 2, ... ----------------
-    const int s = warp;
-    const uint32_t stage = smem_u32(sm.k[s]);
+    // ---------------- gather: warp hw fills rows 16 hw..16 hw + 15 of every tile ----------------
+    // Unit n = 2 gt + hw of the CTA's sequence goes to ring unit n % kUnits.
+    // A unit is free once the compute warps consumed its previous contents
+    // (the Q unit: once they hold Q in registers); the warp does not wait for
+    // its own copies, which complete on the unit's full barrier.
+    const int hw = warp;
     const int j8 = lane & 7;  // 16-byte chunk within a 128-byte run
     const int kq = lane >> 3;  // row within a group of 4
-    StCursor cur = st_start(p, n_items, s);
+    StCursor cur = st_start(p, n_items, 0);
     StCursor nx = cur;
-    st_advance(p, n_items, nx, kStStages);
+    st_advance(p, n_items, nx, 1);
     StCursor nx2 = nx;
-    st_advance(p, n_items, nx2, kStStages);
+    st_advance(p, n_items, nx2, 1);
     int idx_cur = st_index(p, cur, n_items, lane);
     int idx_nx = st_index(p, nx, n_items, lane);
-    uint32_t n = 0;
     bool ok = true;
-    while (cur.item < n_items) {
-      if (n > 0) {
-        if (lane == 0) ok = mbar_wait(empty0 + 8u * s, (n - 1) & 1u, abort_flag);
+    for (uint32_t gt = 0; cur.item < n_items; ++gt) {
+      const uint32_t n = 2u * gt + (uint32_t)hw;
+      const uint32_t u = n % kUnits, use = n / kUnits;
+      const bool q_unit = u == (uint32_t)(2 * kStStages);  // only in the cluster-merge launch
+      if (use > 0 || q_unit) {
+        if (lane == 0) ok = mbar_wait(empty0 + 8u * u, (q_unit ? use : use - 1u) & 1u, abort_flag);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (!ok) break;
       }
-      sm.ids[s][lane] = idx_cur;  // validity is judged from the original index
+      if ((lane >> 4) == hw) sm.ids[u][lane & 15] = idx_cur;  // validity is judged from the original index
       const int row = checked_index(min(max(idx_cur, 0), L - 1), L, p.status);
       const int gb = checked_index(cur.w.batch, p.batch, p.status);
       const __nv_bfloat16* kv_b = p.kv + (size_t)gb * L * kDimLatent;
       const __nv_bfloat16* kr_b = p.k_rope + (size_t)gb * L * kDimRope;
+      const uint32_t unit = st_unit_addr(sm, u);
 #pragma unroll 2
-      for (int i = 0; i < kStBN / 4; ++i) {
-        const int key = kq + 4 * i;
-        const int rk = __shfl_sync(0xffffffffu, row, key);
-        const uint32_t dst = checked_smem(stage + (uint32_t)(key * kStRow + j8 * 8) * 2u, 8u * 128u + 16u, stage,
-                                          (uint32_t)(kStBN * kStRow * 2), p.status);
+      for (int i = 0; i < kStUnitRows / 4; ++i) {
+        const int key = kq + 4 * i;  // row of the unit
+        const int rk = __shfl_sync(0xffffffffu, row, 16 * hw + key);
+        const uint32_t dst = checked_smem(unit + (uint32_t)(key * kStRow + j8 * 8) * 2u, 8u * 128u + 16u, unit,
+                                          kStUnitBytes, p.status);
         const __nv_bfloat16* src = kv_b + (size_t)rk * kDimLatent + j8 * 8;
 #pragma unroll
         for (int kb = 0; kb < 8; ++kb) cp_async_16(dst + kb * 128u, src + kb * 64);
         cp_async_16(dst + 8u * 128u, kr_b + (size_t)rk * kDimRope + j8 * 8);
       }
-      cp_async_commit();
-      const int idx_nx2 = st_index(p, nx2, n_items, lane);  // consumed one round later
-      cp_async_wait<0>();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(full0 + 8u * s);
-      ++n;
+      cp_async_mbar_arrive_noinc(full0 + 8u * u);
+      const int idx_nx2 = st_index(p, nx2, n_items, lane);  // consumed two tiles later
       cur = nx;
       nx = nx2;
-      st_advance(p, n_items, nx2, kStStages);
+      st_advance(p, n_items, nx2, 1);
       idx_cur = idx_nx;
       idx_nx = idx_nx2;
     }
+    cp_async_wait_all();  // no copy into this CTA's shared memory outlives the warp
     if (!ok && lane == 0) report_error(p.status, kErrTimeout);
     if constexpr (kCM) stream_cluster_merge(p, !(*abort_flag) && !*reinterpret_cast<volatile int*>(&sm.stop));
     return;
@@ -279,7 +305,6 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
   const int cw = ctid >> 5;                    // compute warp 0..3
   const int g = lane >> 2;                     // mma group id (row within 8)
   const int tq = lane & 3;                     // thread in group
-  constexpr int kKeysPerWarp = kStBN / 4;      // 8 QK keys per warp
   uint32_t gt = 0;                             // tile counter of this CTA
   bool failed = false;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -310,17 +335,26 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
 #pragma unroll
       for (int ks = 0; ks < kQkSteps; ++ks) ldmatrix_x4(qbase + ks * 32, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
     }
+    if constexpr (kCM) {  // the Q buffer becomes the ring's fifth unit (the CTA's only item)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8u * (uint32_t)(2 * kStStages));
+    }
 
     float acc[16][4];
 #pragma unroll
     for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
     for (int t = 0; t < w.ntiles; ++t, ++gt) {
-      const int s = (int)(gt % kStStages);
-      // stage full: every compute warp waits (bounded); a warp that gives up
+      // the tile's two units (keys 0..15 in ua, 16..31 in ub)
+      const uint32_t n0 = 2u * gt, n1 = n0 + 1u;
+      const uint32_t ua = n0 % kUnits, ub = n1 % kUnits;
+      const uint32_t unit_a = st_unit_addr(sm, ua), unit_b = st_unit_addr(sm, ub);
+      // units full: every compute warp waits (bounded); a warp that gives up
       // flags it and still takes this tile's barriers, and all leave after
       // the last one
-      if (!mbar_wait(full0 + 8u * s, (gt / kStStages) & 1u, abort_flag)) sm.stop = 1;
+      if (!mbar_wait(full0 + 8u * ua, (n0 / kUnits) & 1u, abort_flag) ||
+          !mbar_wait(full0 + 8u * ub, (n1 / kUnits) & 1u, abort_flag))
+        sm.stop = 1;
 
       // ---- partial S = Q.K^T over this warp's dims, all 32 keys ----
       {
@@ -328,20 +362,21 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
 #pragma unroll
         for (int nt = 0; nt < kStBN / 8; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
         // ldmatrix_x4 over 8 keys x 32 dims: b0,b1 = k-step 2j, b2,b3 = k-step 2j+1
-        const uint32_t kbase =
-            smem_u32(sm.k[s]) + ((lane & 7) * kStRow + (lane >> 3) * 8 + cw * 16 * kQkSteps) * 2;
+        const uint32_t koff = (uint32_t)((lane & 7) * kStRow + (lane >> 3) * 8 + cw * 16 * kQkSteps) * 2u;
 #pragma unroll
         for (int nt = 0; nt < kStBN / 8; ++nt) {
+          // keys 8 nt..8 nt + 7: rows 8 (nt % 2).. of unit a (nt < 2) or b
+          const uint32_t kbase = (nt < 2 ? unit_a : unit_b) + koff + (uint32_t)((nt & 1) * 8 * kStRow) * 2u;
 #pragma unroll
           for (int j = 0; j < kQkSteps / 2; ++j) {
             uint32_t b0, b1, b2, b3;
-            ldmatrix_x4(kbase + (nt * 8 * kStRow + j * 32) * 2, b0, b1, b2, b3);
+            ldmatrix_x4(kbase + (j * 32) * 2, b0, b1, b2, b3);
             mma_bf16_16816(d[nt], qf[2 * j][0], qf[2 * j][1], qf[2 * j][2], qf[2 * j][3], b0, b1);
             mma_bf16_16816(d[nt], qf[2 * j + 1][0], qf[2 * j + 1][1], qf[2 * j + 1][2], qf[2 * j + 1][3], b2, b3);
           }
           // odd step count: the last 16 dims with an x2 load (8 keys x 16 dims)
           uint32_t b0, b1;
-          ldmatrix_x2(kbase + (nt * 8 * kStRow + (kQkSteps - 1) * 16) * 2, b0, b1);
+          ldmatrix_x2(kbase + ((kQkSteps - 1) * 16) * 2, b0, b1);
           mma_bf16_16816(d[nt], qf[kQkSteps - 1][0], qf[kQkSteps - 1][1], qf[kQkSteps - 1][2],
                          qf[kQkSteps - 1][3], b0, b1);
         }
@@ -368,12 +403,14 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
         __syncwarp();
         float x[kCols];
         float mx = -INFINITY;
+        static_assert(kStUnitRows % kCols == 0, "a thread's columns lie in one unit");
+        const int* const ids_c = c0 < kStUnitRows ? &sm.ids[ua][c0] : &sm.ids[ub][c0 - kStUnitRows];
 #pragma unroll
         for (int i = 0; i < kCols; ++i) {
           const int col = c0 + i;
           const float sc = sm.s[0][r * kStBN + col] + sm.s[1][r * kStBN + col] + sm.s[2][r * kStBN + col] +
                            sm.s[3][r * kStBN + col];
-          const int id = sm.ids[s][col];
+          const int id = ids_c[i];
           x[i] = ((id >= 0) & (id < L)) ? sc : -INFINITY;
           mx = fmaxf(mx, x[i]);
         }
@@ -416,24 +453,28 @@ __global__ void __launch_bounds__(kStThreads, 2) fwd_stream_kernel(const FwdPara
         }
         const uint32_t pbase =
             smem_u32(sm.p) + (((lane & 7) + ((lane >> 3) & 1) * 8) * kStPRow + (lane >> 4) * 8) * 2;
-        const uint32_t vbase = smem_u32(sm.k[s]) +
-                               (((lane & 7) + ((lane >> 3) & 1) * 8) * kStRow + cw * 128 + (lane >> 4) * 8) * 2;
+        const uint32_t voff =
+            (uint32_t)((((lane & 7) + ((lane >> 3) & 1) * 8) * kStRow + cw * 128 + (lane >> 4) * 8) * 2);
 #pragma unroll
-        for (int kk = 0; kk < kStBN / 16; ++kk) {
+        for (int kk = 0; kk < kStBN / 16; ++kk) {  // keys 16 kk..16 kk + 15: unit a, then b
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4(pbase + kk * 32, a0, a1, a2, a3);
+          const uint32_t vbase = (kk == 0 ? unit_a : unit_b) + voff;
 #pragma unroll
           for (int jp = 0; jp < 8; ++jp) {
             uint32_t b0, b1, b2, b3;
-            ldmatrix_x4_trans(vbase + (kk * 16 * kStRow + jp * 16) * 2, b0, b1, b2, b3);
+            ldmatrix_x4_trans(vbase + (jp * 16) * 2, b0, b1, b2, b3);
             mma_bf16_16816(acc[2 * jp], a0, a1, a2, a3, b0, b1);
             mma_bf16_16816(acc[2 * jp + 1], a0, a1, a2, a3, b2, b3);
           }
         }
       }
-      // this warp is done with stage s
+      // this warp is done with the tile's units
       __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8u * s);
+      if (lane == 0) {
+        mbar_arrive(empty0 + 8u * ua);
+        mbar_arrive(empty0 + 8u * ub);
+      }
       if (*reinterpret_cast<volatile int*>(&sm.stop)) {  // set before the softmax barrier
         failed = true;
         break;
