@@ -49,31 +49,35 @@ CONFIGS = {
 DEFAULT_CONFIG = "prefill_h128"
 
 # Dominant-kernel DRAM traffic per launch (dram__bytes_read.sum +
-# dram__bytes_write.sum) from ncu captures of the default launch on the
-# uniform index variant, as a model of a rank's launch:
+# dram__bytes_write.sum), from one-pass ncu captures (`--cache-control none`)
+# of timed-loop launches of this script, i.e. right after the 256 MiB write
+# that flushes the L2: the writes include the flush buffer's dirty lines that
+# the launch evicts (a decode launch writes back about as many bytes as it
+# brings into the L2). Modelled per rank on the uniform index variant as
 #   traffic = replicated + per_query * (queries of the rank)
 # where `replicated` is what every rank reads whatever its query count (kv
 # rows that stay L2-resident after their first read). The bench reports
 # None for any other variant, shape or launch entry.
 TRAFFIC_MODEL = {
-    # fwd_pair_kernel, full prefill_h128 launch (1-pass capture of ten
-    # launches): 10.49 GB read + 2.175 GB written. kv is re-read from DRAM in
-    # proportion to the queries (75.5 MB of kv per batch row does not stay in
-    # the L2 next to the streamed q and outputs), so it all scales per query.
-    "prefill_h128": (0.0, (10.49e9 + 2.175e9) / 16384),
-    # union launch's fwd_pair_kernel, 1024-query capture of prefill_tp8:
-    # 32.2 MB read + 0.17 MB written, of which the 9.4 MB kv + k_rope is
-    # read once (it stays L2-resident) and the rest scales with the queries.
-    "prefill_tp8": (9.4e6, (32.2e6 - 9.4e6 + 0.17e6) / 1024),
-    # fwd_stream_kernel (cluster merge), capture of ten full decode_tp8
-    # launches: 152.8 MB read + 0.48 MB written.
-    "decode_tp8": (0.0, (152.8e6 + 0.48e6) / 64),
-    # fwd_umma_kernel (cluster merge), capture of ten full decode_b8 launches:
-    # 39.10 MB read + 0.06 MB written (the FP32 partials stay in the L2).
-    "decode_b8": (0.0, (39.10e6 + 0.06e6) / 16),
-    # fwd_umma_kernel (cluster merge, split 16), capture of ten full
-    # decode_b1 launches: 2.62 MB read, nothing written back to DRAM.
-    "decode_b1": (0.0, 2.62e6),
+    # fwd_pair_kernel, prefill_h128: 10.506 GB read + 2.239 GB written (the
+    # 2.15 GB of outputs and the flush's dirty lines). kv is re-read in
+    # proportion to the queries (75.5 MB of kv per batch row does not stay
+    # in the L2 next to the streamed q and outputs), so it all scales per query.
+    "prefill_h128": (0.0, (10.506e9 + 2.239e9) / 16384),
+    # union launch's fwd_pair_kernel, prefill_tp8: 95.1 MB read + 84.1 MB
+    # written (67 MB of outputs and dirty lines written back), of which the
+    # 9.4 MB kv + k_rope is read once (it stays L2-resident) and the rest
+    # scales with the queries.
+    "prefill_tp8": (9.4e6, (95.1e6 + 84.1e6 - 9.4e6) / 4096),
+    # fwd_stream_kernel (cluster merge), decode_tp8: 152.7 MB read + 61.6 MB
+    # of dirty lines written back.
+    "decode_tp8": (0.0, (152.7e6 + 61.6e6) / 64),
+    # fwd_umma_kernel (cluster merge), decode_b8: 39.1 MB read + 33.2 MB
+    # written back (the FP32 partials themselves stay in the L2).
+    "decode_b8": (0.0, (39.1e6 + 33.2e6) / 16),
+    # fwd_umma_kernel (cluster merge, split 16), decode_b1: 2.57 MB read +
+    # 5.72 MB written back.
+    "decode_b1": (0.0, 2.57e6 + 5.72e6),
 }
 
 
@@ -608,7 +612,7 @@ def main():
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)",
                      "traffic": traffic_bytes(args.config, args.variant, bool(args.shape or args.tuning), hi - lo),
-                     "traffic_source": "ncu capture of the default launch (uniform indices), modelled per rank"},
+                     "traffic_source": "ncu capture of timed-loop launches of the default launch (uniform indices, after the L2 write flush), modelled per rank"},
         "e2e": {"value": e2e_ms * 1e3, "unit": "us/call", "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": d2h_bytes, "steps": e2e_steps,
                 "mode": "pipelined: inputs in / forward / outputs out on three streams, two buffer sets"},

@@ -12,8 +12,9 @@
 // a warp runs ahead of the compute warps as far as the ring allows; two CTAs
 // share an SM. The ring has four units in the stage buffers plus, in the
 // cluster-merge launch (one item per CTA), a fifth in the Q buffer once the
-// compute warps hold Q in registers: 2.5 tiles of rows in flight instead of
-// two, which is what bounds the tile rate when the rows come from HBM.
+// compute warps hold Q in registers: up to 2.5 tiles of rows gathered ahead
+// instead of two (the rows' latency sets the tile rate when they come from
+// HBM).
 //
 // The four compute warps run the reference's per-tile dataflow
 // (dsa/workspace.py:242-318) with warp-level m16n8k16 BF16 MMAs: S = Q.K^T
