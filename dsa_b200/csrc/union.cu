@@ -85,15 +85,15 @@ __global__ void __launch_bounds__(kUnionThreads, 2) union_build_kernel(const int
   int32_t* bent = uent + (size_t)blk * ucap;
   const int n_ids = QPB * topk;
   const bool cached = n_ids <= kIdsCached * kUnionThreads && length < (int)kNoKey;
-  // cached path: thread tid holds slots tid / QPB + i * (1024 / QPB) of query
-  // tid % QPB, so its query needs no division
+  // cached path: thread tid holds slots tid % kPerQuery + i * kPerQuery of
+  // query tid / kPerQuery, so a warp reads 32 consecutive indices of one row
   constexpr int kPerQuery = kUnionThreads / QPB;
-  const int cq = tid % QPB;
+  const int cq = tid / kPerQuery;
   uint32_t idr[kIdsCached / 2];  // two 16-bit keys per register
   if (cached) {
 #pragma unroll
     for (int i = 0; i < kIdsCached; ++i) {
-      const int j = tid / QPB + i * kPerQuery;
+      const int j = tid % kPerQuery + i * kPerQuery;
       const int idx = j < topk ? __ldg(bids + (size_t)cq * topk + j) : -1;
       const uint32_t k = (idx >= 0 && idx < length) ? (uint32_t)idx : kNoKey;
       if (i & 1)

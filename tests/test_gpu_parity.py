@@ -66,6 +66,19 @@ def test_explicit_splits(cuda_lib, bn, split):
     _check(out, oracle.reference_forward(*data))
 
 
+@pytest.mark.parametrize("topk", [64, 80])
+def test_stream_items_per_cta(cuda_lib, topk):
+    """The persistent stream launch (split 1) with more items than resident
+    CTAs: each CTA runs several items, and its gather ring carries on from
+    one item's last tile into the next item's first (odd tile counts too)."""
+    shape = (1, 700, 16, 2048, topk)
+    data = oracle.make_inputs(shape, 11, "normal")
+    out, kernels = dsa_b200.forward(*_gpu(data), config=dsa_b200.Tuning(16, 32, 1), return_kernels=True)
+    torch.cuda.synchronize()
+    assert [k.name for k in kernels] == ["dsa_fwd_stream"], kernels
+    _check(out, oracle.reference_forward(*data))
+
+
 def test_invalid_and_duplicate_index_semantics(cuda_lib):
     shape = (1, 1, 16, 256, 8)
     q, kv, qr, kr, _ = oracle.make_inputs(shape, 7, "normal")
