@@ -575,7 +575,7 @@ def main():
     rank_share = (hi - lo) / (b * s)
     per_launch_flops = flops * rank_share
     per_launch_bytes = gathered * rank_share
-    # Decode shapes are judged on gathered bytes against HBM, prefill shapes
+    # Decode shapes are measured on gathered bytes against HBM, prefill shapes
     # (many queries per call) on FLOPs against the BF16 tensor peak.
     if s >= 64 or (args.config.startswith("prefill")):
         bound, achieved, peak, unit = "tensor", per_launch_flops / (ms_per_step * 1e-3) / 1e12, tf_peak, "TFLOP/s"
