@@ -2,7 +2,8 @@
 """Sparse-MLA forward benchmark on B200 (one process per GPU).
 
 ``python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME]
-[--variant uniform|peaked|duplicates] [--impl ours|reference]``
+[--variant uniform|peaked|duplicates] [--impl ours|reference]
+[--inputs device|reference]``
 
 A step is one full ``dsa_b200.forward`` call (main kernel + merge when
 split > 1) over the config's synthetic inputs. With N ranks (torchrun), the
@@ -17,6 +18,14 @@ Total work is fixed as N grows ("strong" scaling).
 ``--impl reference`` times the reference's own FP32 math (the CPU oracle,
 tools/review.py:123-145 of CHNJZ/dsa) on all host cores, on a bounded
 sample of the same workload per step, scaled to a full call.
+
+Inputs are drawn on the device by default (same shapes and distributions as
+the reference's generator, seconds even for prefill_h128); ``--inputs
+reference`` draws them in the reference's own order on the CPU instead
+(tools/review.py:35-61: one generator seeded with the config's seed, randn
+for q, kv, q_rope, k_rope, then randperm(L)[:TOPK] per query), so the values
+are the ones the reference's runs for that seed use (uniform variant only;
+minutes of host time for prefill_h128).
 """
 from __future__ import annotations
 
@@ -153,6 +162,35 @@ def make_device_indices(batch, queries, length, topk, seed, variant, device):
     else:
         raise ValueError(variant)
     return out.reshape(batch, queries, 1, topk)
+
+
+def make_reference_order_inputs(shape, seed=SEED, device="cuda"):
+    """The inputs the reference's generator gives for ``seed``
+    (tools/review.py:35-61): one CPU generator, N(0,1) draws for q, kv,
+    q_rope and k_rope in that order (rounded to BF16), then
+    randperm(L)[:TOPK] for every (b, s) in order; copied to ``device``."""
+    b, s, h, length, k = shape
+    g = torch.Generator().manual_seed(seed)
+
+    def normal(*dims):
+        return torch.randn(dims, generator=g).bfloat16().to(device)
+
+    q = normal(b, s, h, 512)
+    kv = normal(b, length, 1, 512)
+    q_rope = normal(b, s, h, 64)
+    k_rope = normal(b, length, 1, 64)
+    ids = torch.empty((b * s, k), dtype=torch.int32)
+    for r in range(b * s):
+        ids[r] = torch.randperm(length, generator=g)[:k]
+    return q, kv, q_rope, k_rope, ids.reshape(b, s, 1, k).to(device)
+
+
+def make_inputs_for(args, shape, device):
+    if args.inputs == "reference":
+        if args.variant != "uniform":
+            raise SystemExit("--inputs reference draws the reference's uniform indices only")
+        return make_reference_order_inputs(shape, SEED, device)
+    return make_device_inputs(shape, SEED, args.variant, device)
 
 
 def make_device_inputs(shape, seed=SEED, variant="uniform", device="cuda"):
@@ -348,7 +386,7 @@ def run_reference(args, shape):
     if rank != 0:
         return 0
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    data = make_device_inputs(shape, SEED, args.variant, dev)
+    data = make_inputs_for(args, shape, dev)
     b, s, h, length, k = shape
     sample = CpuSample(data, shape)
     data = None
@@ -386,6 +424,8 @@ def main():
     ap.add_argument("--shape", default=None,
                     help="B,SQ,H,L,TOPK override (a reduced case for profiling; workload 'custom')")
     ap.add_argument("--variant", default="uniform", choices=("uniform", "peaked", "duplicates"))
+    ap.add_argument("--inputs", default="device", choices=("device", "reference"),
+                    help="draw the inputs on the device (default) or in the reference's generator order on the CPU")
     ap.add_argument("--tuning", default=None,
                     help="bm,bn,split[,pv_cols] launch entry instead of the shape-keyed default "
                          "(selects a kernel family, e.g. 128,32,1,256 for the split-V family)")
@@ -412,7 +452,7 @@ def main():
     world, rank, local = init_dist()
     device = torch.device("cuda", local)
     b, s, h, length, k = shape
-    data = make_device_inputs(shape, SEED, args.variant, device)
+    data = make_inputs_for(args, shape, device)
     lo, hi = sharded.shard_bounds(b * s, world, rank)
     pieces = sharded.shard_pieces(s, lo, hi)
     views = [(data[0][b0:b1, s0:s1], data[1][b0:b1], data[2][b0:b1, s0:s1], data[3][b0:b1],
@@ -594,9 +634,10 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) BF16 q/kv/q_rope/k_rope, int32 top-k indices "
-                f"({args.variant}), generated on the device",
+                + (f"({args.variant}), generated on the device" if args.inputs == "device" else
+                   "(uniform), drawn in the reference's generator order (tools/review.py:35-61) on the CPU"),
         "config": {"workload": args.config, "B": b, "SQ": s, "H": h, "L": length, "TOPK": k,
-                   "index_variant": args.variant, "seed": SEED,
+                   "index_variant": args.variant, "seed": SEED, "inputs": args.inputs,
                    "parallelism": f"query-shard x{world}, kv replicated",
                    "l2": "flushed between timed iterations (256 MiB write outside the events)",
                    "timed": ("direct launches of ForwardPlan.run" if args.direct
@@ -629,7 +670,7 @@ def main():
         # method), in a fresh child process after this process's GPU timing
         cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference", "--config",
                args.config if not args.shape else DEFAULT_CONFIG, "--variant", args.variant, "--steps", "5",
-               "--warmup", "3"] + (["--shape", args.shape] if args.shape else [])
+               "--warmup", "3", "--inputs", args.inputs] + (["--shape", args.shape] if args.shape else [])
         env = dict(os.environ, WORLD_SIZE="1", RANK="0", LOCAL_RANK="0")
         res = subprocess.run(cmd, capture_output=True, text=True, env=env)
         ref = None

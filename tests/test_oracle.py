@@ -199,3 +199,14 @@ def test_oracle_maximum_rounding_is_absolute():
     assert float(err.max()) < 1e-6
     assert float((err / exact.abs()).max()) > 1e-5
     assert float((err / exact.abs().clamp_min(1.0)).max()) < 1e-6
+
+
+def test_bench_reference_order_inputs_match_the_reference_generator():
+    """``bench.py --inputs reference`` draws exactly the reference's inputs
+    for a seed (tools/review.py:35-61), as the oracle's restatement does."""
+    import bench
+    shape = (2, 3, 16, 300, 40)
+    got = bench.make_reference_order_inputs(shape, 20261103, "cpu")
+    want = oracle.make_inputs(shape, 20261103, "normal")
+    for a, b in zip(got, want):
+        assert a.dtype == b.dtype and torch.equal(a, b)
