@@ -382,6 +382,43 @@ __device__ __forceinline__ void store_bf16_row32(__nv_bfloat16* dst, const uint3
   }
 }
 
+// store_bf16_row32 for a lane pair, in two steps. Pack: this lane's 32 FP32
+// values (its row) * rl -> BF16, exchanged with the partner lane (lane ^ 1)
+// so that a[] holds 32 bytes of the pair's even row and b[] 32 bytes of its
+// odd row (bytes 0..31 in the even lane, 32..63 in the odd lane). Store:
+// each store instruction then writes 64 contiguous bytes of one row per lane
+// pair (16 rows x 64 B per warp instruction instead of 32 rows x 32 B:
+// ~1.5x the per-SM store rate). All 32 lanes take part in the pack.
+__device__ __forceinline__ void pack_bf16_row32_paired(const uint32_t* o, float rl, uint32_t* a, uint32_t* b) {
+  const bool odd = (threadIdx.x & 1u) != 0u;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t lo = pack_bf16x2(__uint_as_float(o[2 * k]) * rl, __uint_as_float(o[2 * k + 1]) * rl);
+    const uint32_t hi = pack_bf16x2(__uint_as_float(o[16 + 2 * k]) * rl, __uint_as_float(o[17 + 2 * k]) * rl);
+    const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
+    a[k] = odd ? got : lo;
+    b[k] = odd ? hi : got;
+  }
+}
+// `dst_even`: the chunk's first element in the pair's even row; the odd row
+// starts `row_stride` elements later.
+__device__ __forceinline__ void store_bf16_row32_paired(__nv_bfloat16* dst_even, size_t row_stride, const uint32_t* a,
+                                                        const uint32_t* b, bool wide) {
+  __nv_bfloat16* const de = dst_even + ((threadIdx.x & 1u) ? 16 : 0);
+  __nv_bfloat16* const dod = de + row_stride;
+  if (wide) {
+    st_global_v8(de, a);
+    st_global_v8(dod, b);
+  } else {
+    uint4* const e4 = reinterpret_cast<uint4*>(de);
+    uint4* const o4 = reinterpret_cast<uint4*>(dod);
+    e4[0] = make_uint4(a[0], a[1], a[2], a[3]);
+    e4[1] = make_uint4(a[4], a[5], a[6], a[7]);
+    o4[0] = make_uint4(b[0], b[1], b[2], b[3]);
+    o4[1] = make_uint4(b[4], b[5], b[6], b[7]);
+  }
+}
+
 // 32 FP32 values * f -> dst (128 B of an FP32 partial row); 32-byte stores
 // when dst is 32-byte aligned (`wide`), 16-byte stores otherwise.
 __device__ __forceinline__ void store_f32_row32(float* dst, const uint32_t* o, float f, bool wide) {
