@@ -205,6 +205,49 @@ def test_c_abi_direct_call_matches_api(cuda_lib):
     assert torch.equal(out, ref[0]) and torch.equal(mx, ref[1]) and torch.equal(sm, ref[2])
 
 
+def _abi_forward(cuda_lib, data, shape, launch, out_offset):
+    """One call through the C ABI with the output starting `out_offset`
+    BF16 elements into its buffer."""
+    b, s, h, _, _ = shape
+    buf = torch.empty(b * s * h * 512 + out_offset, dtype=torch.bfloat16, device="cuda")
+    out = buf[out_offset:].view(b, s, h, 512)
+    mx = torch.empty((b, 1, s, h), device="cuda")
+    sm = torch.empty_like(mx)
+    args = _native.FwdArgs()
+    args.q, args.kv, args.q_rope, args.k_rope, args.indices = [t.data_ptr() for t in data]
+    args.output, args.softmax_max, args.softmax_sum = out.data_ptr(), mx.data_ptr(), sm.data_ptr()
+    args.batch, args.queries, args.heads, args.length, args.topk = shape
+    args.launch = launch
+    ws = cuda_lib.dsa_fwd_workspace_bytes(ctypes.byref(args))
+    wbuf = torch.empty(max(ws, 1), dtype=torch.uint8, device="cuda")
+    args.workspace, args.workspace_bytes = wbuf.data_ptr(), ws
+    assert cuda_lib.dsa_sparse_mla_fwd(ctypes.byref(args), torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    return out.clone(), mx, sm
+
+
+@pytest.mark.parametrize("shape,launch", [
+    ((1, 80, 128, 4096, 256), (_native.FAMILY_UMMA_PAIR, 128, 32, 1)),   # pair, paired row stores
+    ((1, 2, 128, 4096, 256), (_native.FAMILY_UMMA, 128, 32, 1)),          # split-V, row stores
+    ((2, 1, 128, 4096, 512), (_native.FAMILY_UMMA, 128, 32, 4)),          # split-V, merge in the cluster
+    ((1, 64, 16, 1024, 256), (_native.FAMILY_PAIR_UNION, 128, 32, 1)),    # union launch
+    ((2, 3, 16, 4096, 256), (_native.FAMILY_STREAM, 16, 32, 1)),
+    ((2, 1, 16, 4096, 1024), (_native.FAMILY_STREAM, 16, 32, 4)),        # stream, merge in the cluster
+    ((2, 3, 16, 4096, 256), (_native.FAMILY_WARP_MMA, 16, 32, 1)),
+], ids=["pair", "split-V", "split-V-cluster", "union", "stream", "stream-cluster", "warp-MMA"])
+def test_output_16_byte_aligned(cuda_lib, shape, launch):
+    """The C ABI accepts an output that is 16- but not 32-byte aligned: the
+    families then take their 16-byte store paths, with bit-identical
+    results."""
+    data = _gpu(oracle.make_inputs(shape, 13, "normal"))
+    la = _native.Launch(*launch)
+    aligned = _abi_forward(cuda_lib, data, shape, la, 0)
+    offset = _abi_forward(cuda_lib, data, shape, la, 8)  # 16 bytes into a 512-byte aligned buffer
+    for x, y in zip(aligned, offset):
+        assert torch.equal(x, y)
+    _check(offset, oracle.reference_forward(*[t.cpu() for t in data]))
+
+
 def test_workspace_too_small_is_reported(cuda_lib):
     shape = (1, 1, 32, 1024, 256)
     data = _gpu(oracle.make_inputs(shape, 9, "normal"))
