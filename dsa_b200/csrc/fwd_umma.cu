@@ -212,19 +212,16 @@ __device__ __forceinline__ void store_o_part(const FwdParams& p, const Item& w, 
     // correctly rounded reciprocal (within an FP32 ulp of O / l); a row
     // without a valid index (l == 0) is written as 0
     const float rl = l > 0.f ? __frcp_rn(l) : 0.f;
-    __nv_bfloat16* dst = p.out + ((size_t)w.token * kUmHeads + row) * kDimLatent + col0;
+    // the lane pair's two rows (row and row ^ 1; lane parity = row parity)
+    __nv_bfloat16* dst = p.out + ((size_t)w.token * kUmHeads + (row & ~1)) * kDimLatent + col0;
     const bool wide = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;  // rows are 1024 B apart
-    tmem_ld32(o_lane + cb0, oa);
 #pragma unroll 1
-    for (int cb = cb0; cb < cb1; cb += 64) {
-      tmem_wait_ld_regs32(oa);
-      const bool more = cb + 32 < cb1;
-      if (more) tmem_ld32(o_lane + cb + 32, ob);
-      store_bf16_row32(dst + cb, oa, rl, wide);
-      if (!more) break;
-      tmem_wait_ld_regs32(ob);
-      if (cb + 64 < cb1) tmem_ld32(o_lane + cb + 64, oa);
-      store_bf16_row32(dst + cb + 32, ob, rl, wide);
+    for (int cb = cb0; cb < cb1; cb += 32) {
+      tmem_ld32(o_lane + cb, oa);
+      tmem_wait_ld();
+      uint32_t a[8], b[8];
+      pack_bf16_row32_paired(oa, rl, a, b);
+      store_bf16_row32_paired(dst + cb, kDimLatent, a, b, wide);
     }
   } else {
     float* dst = p.part_num + (((size_t)w.token * p.split + w.sp) * kUmHeads + row) * kDimLatent + col0;
